@@ -1,0 +1,261 @@
+// capi_ops.cpp — extern "C" op entry points: argument validation, then the launchers.
+// Validation mirrors the reference's checks where it has them (shape errors are
+// std::invalid_argument there: src/ops/cuda/cuda_matrix_ops.cu:314-319, :365-373,
+// :470-481; src/ops/cuda/cuda_attention_ops.cu:182-187) and returns
+// FE_ERR_INVALID_ARGUMENT instead of throwing or exiting.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "fe_internal.h"
+
+using fe::fail;
+
+namespace {
+
+inline cudaStream_t cs(fe_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline fe_status done(cudaError_t e, const char *what) { return fe::check_cuda(e, what); }
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+fe_status fe_sgemm_nn(const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                      fe_stream_t stream)
+{
+    if (m < 0 || n < 0 || k < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nn: negative size");
+    if ((m * k) && (!c || (n && (!a || !b)))) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nn: null pointer");
+    return done(fe::launch_sgemm(a, b, nullptr, c, m, n, k, false, cs(stream)), "fe_sgemm_nn");
+}
+
+fe_status fe_sgemm_nt(const float *a, const float *b, const float *bias, float *c, int64_t m, int64_t n,
+                      int64_t k, fe_stream_t stream)
+{
+    if (m < 0 || n < 0 || k < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nt: negative size");
+    if ((m * k) && (!c || (n && (!a || !b)))) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nt: null pointer");
+    return done(fe::launch_sgemm(a, b, bias, c, m, n, k, true, cs(stream)), "fe_sgemm_nt");
+}
+
+static fe_status unary(int op, const float *x, float *y, int64_t count, fe_stream_t stream, const char *name)
+{
+    if (count < 0) return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": negative count");
+    if (count && (!x || !y)) return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+    return done(fe::launch_unary(op, x, y, count, cs(stream)), name);
+}
+
+fe_status fe_gelu_f32(const float *x, float *y, int64_t count, fe_stream_t s) { return unary(FE_ACT_GELU, x, y, count, s, "fe_gelu_f32"); }
+fe_status fe_relu_f32(const float *x, float *y, int64_t count, fe_stream_t s) { return unary(FE_ACT_RELU, x, y, count, s, "fe_relu_f32"); }
+fe_status fe_swish_f32(const float *x, float *y, int64_t count, fe_stream_t s) { return unary(FE_ACT_SWISH, x, y, count, s, "fe_swish_f32"); }
+
+fe_status fe_layer_norm_f32(const float *x, const float *gamma, const float *beta, float *y, int64_t rows,
+                            int64_t dim, float eps, fe_stream_t stream)
+{
+    if (rows < 0 || dim <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_layer_norm_f32: bad shape");
+    if (rows && (!x || !gamma || !beta || !y)) return fail(FE_ERR_INVALID_ARGUMENT, "fe_layer_norm_f32: null pointer");
+    if (rows > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_layer_norm_f32: too many rows");
+    return done(fe::launch_layer_norm_f32(x, gamma, beta, y, rows, dim, eps, cs(stream)), "fe_layer_norm_f32");
+}
+
+fe_status fe_rms_norm_f32(const float *x, const float *weight, float *y, int64_t rows, int64_t dim, float eps,
+                          fe_stream_t stream)
+{
+    if (rows < 0 || dim <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_norm_f32: bad shape");
+    if (rows && (!x || !weight || !y)) return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_norm_f32: null pointer");
+    if (rows > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_rms_norm_f32: too many rows");
+    return done(fe::launch_rms_norm_f32(x, weight, y, rows, dim, eps, cs(stream)), "fe_rms_norm_f32");
+}
+
+fe_status fe_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t dim, fe_stream_t stream)
+{
+    if (rows < 0 || dim <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_softmax_rows_f32: bad shape");
+    if (rows && (!x || !y)) return fail(FE_ERR_INVALID_ARGUMENT, "fe_softmax_rows_f32: null pointer");
+    if (rows > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_softmax_rows_f32: too many rows");
+    return done(fe::launch_softmax_rows_f32(x, y, rows, dim, cs(stream)), "fe_softmax_rows_f32");
+}
+
+fe_status fe_softmax_scores_inplace_f32(float *scores, int64_t heads, int64_t seq_len, fe_stream_t stream)
+{
+    if (heads < 0 || seq_len < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_softmax_scores_inplace_f32: bad shape");
+    if (heads * seq_len == 0) return FE_OK;
+    if (!scores) return fail(FE_ERR_INVALID_ARGUMENT, "fe_softmax_scores_inplace_f32: null pointer");
+    return done(fe::launch_softmax_rows_f32(scores, scores, heads * seq_len, seq_len, cs(stream)),
+                "fe_softmax_scores_inplace_f32");
+}
+
+size_t fe_mha_f32_workspace_bytes(int64_t seq_len, int64_t dim, int64_t heads)
+{
+    (void)heads;
+    if (seq_len <= 0 || dim <= 0) return 0;
+    return static_cast<size_t>(3 * seq_len * dim) * sizeof(float);
+}
+
+fe_status fe_mha_f32(const float *x, const float *wq, const float *wk, const float *wv, const float *bq,
+                     const float *bk, const float *bv, float *out, int64_t seq_len, int64_t dim, int64_t heads,
+                     void *workspace, size_t workspace_bytes, fe_stream_t stream)
+{
+    if (heads <= 0 || dim <= 0 || seq_len < 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_mha_f32: bad shape");
+    if (dim % heads != 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "Embedding dimension must be divisible by number of heads");
+    if (seq_len == 0) return FE_OK;
+    if (!x || !wq || !wk || !wv || !bq || !bk || !bv || !out)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_mha_f32: null pointer");
+    if (!workspace || workspace_bytes < fe_mha_f32_workspace_bytes(seq_len, dim, heads))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_mha_f32: workspace too small");
+    if (seq_len > 0xffff || static_cast<size_t>(seq_len) * 4 > 200 * 1024)
+        return fail(FE_ERR_UNSUPPORTED, "fe_mha_f32: sequence too long for the fp32 path");
+    float *q = static_cast<float *>(workspace);
+    float *k = q + seq_len * dim;
+    float *v = k + seq_len * dim;
+    cudaStream_t s = cs(stream);
+    FE_TRY_CUDA(fe::launch_sgemm(x, wq, bq, q, seq_len, dim, dim, true, s));
+    FE_TRY_CUDA(fe::launch_sgemm(x, wk, bk, k, seq_len, dim, dim, true, s));
+    FE_TRY_CUDA(fe::launch_sgemm(x, wv, bv, v, seq_len, dim, dim, true, s));
+    return done(fe::launch_mha_core_f32(q, k, v, out, seq_len, dim, heads, s), "fe_mha_f32");
+}
+
+fe_status fe_linear_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
+                         int64_t m, int64_t n, int64_t k, fe_epilogue epilogue, fe_dtype y_dtype,
+                         fe_stream_t stream)
+{
+    if (m < 0 || n <= 0 || k <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: bad shape");
+    if (k % 8 != 0 || n % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: k and n must be multiples of 8");
+    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_linear_bf16: size too large");
+    if (epilogue < FE_EPI_NONE || epilogue > FE_EPI_BIAS_RESIDUAL)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: unknown epilogue");
+    if (y_dtype != FE_DTYPE_F32 && y_dtype != FE_DTYPE_BF16)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: unknown output dtype");
+    if (epilogue == FE_EPI_BIAS_RESIDUAL && y_dtype != FE_DTYPE_F32)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: the residual epilogue writes fp32");
+    if (m == 0) return FE_OK;
+    if (!x || !w || !y) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: null pointer");
+    if (epilogue != FE_EPI_NONE && !bias) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: epilogue needs a bias");
+    if (epilogue == FE_EPI_BIAS_RESIDUAL && !residual)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: residual epilogue needs a residual");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias && !aligned16(bias)) ||
+        (residual && !aligned16(residual)))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: pointers must be 16-byte aligned");
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_linear_bf16(x, w, bias, residual, y, m, n, k, epilogue, y_dtype,
+                                           reinterpret_cast<cudaStream_t>(stream), &st);
+    if (st != FE_OK) return st;
+    return done(e, "fe_linear_bf16");
+}
+
+fe_status fe_attention_varlen_bf16(const void *qkv, const int32_t *cu_seqlens, int32_t batch, int32_t max_len,
+                                   int32_t heads, int32_t head_dim, void *out, int64_t total_tokens,
+                                   fe_stream_t stream)
+{
+    if (batch < 0 || max_len < 0 || heads <= 0 || total_tokens < 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_bf16: bad shape");
+    if (head_dim != 64) return fail(FE_ERR_UNSUPPORTED, "fe_attention_varlen_bf16: head_dim must be 64");
+    if (max_len > 4096 || heads > 65535 || batch > 65535)
+        return fail(FE_ERR_UNSUPPORTED, "fe_attention_varlen_bf16: batch, heads or max_len too large");
+    if (batch == 0 || total_tokens == 0) return FE_OK;
+    if (!qkv || !cu_seqlens || !out) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_bf16: null pointer");
+    if (!aligned16(qkv) || !aligned16(out))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_bf16: pointers must be 16-byte aligned");
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_attention_varlen(qkv, cu_seqlens, batch, max_len, heads, head_dim, out, total_tokens,
+                                                reinterpret_cast<cudaStream_t>(stream), &st);
+    if (st != FE_OK) return st;
+    return done(e, "fe_attention_varlen_bf16");
+}
+
+static bool supported_row_dim(int32_t dim) { return dim > 0 && dim % 128 == 0 && (dim / 128) <= 16; }
+
+fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int32_t batch, int64_t total_tokens,
+                             const float *word, const float *pos, const float *type, const float *gamma,
+                             const float *beta, int32_t dim, int32_t vocab, int32_t max_pos, float eps, float *h32,
+                             void *h16, fe_stream_t stream)
+{
+    if (batch < 0 || total_tokens < 0 || vocab <= 0 || max_pos <= 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm: bad shape");
+    const int v = dim / 128;
+    if (!supported_row_dim(dim) || !(v == 2 || v == 3 || v == 4 || v == 6 || v == 8 || v == 12 || v == 16))
+        return fail(FE_ERR_UNSUPPORTED, "fe_embed_layernorm: dim must be 256, 384, 512, 768, 1024, 1536 or 2048");
+    if (total_tokens == 0) return FE_OK;
+    if (batch == 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm: tokens without sentences");
+    if (!ids || !cu_seqlens || !word || !pos || !type || !gamma || !beta || !h32)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm: null pointer");
+    return done(fe::launch_embed_layernorm(ids, cu_seqlens, batch, total_tokens, word, pos, type, gamma, beta, dim,
+                                           vocab, max_pos, eps, h32, h16, reinterpret_cast<cudaStream_t>(stream)),
+                "fe_embed_layernorm");
+}
+
+fe_status fe_layernorm_dual(const float *x, const float *gamma, const float *beta, float *h32, void *h16,
+                            int64_t rows, int32_t dim, float eps, fe_stream_t stream)
+{
+    if (rows < 0 || dim <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_layernorm_dual: bad shape");
+    if (rows > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_layernorm_dual: too many rows");
+    if (rows == 0) return FE_OK;
+    if (!x || !gamma || !beta || !h32) return fail(FE_ERR_INVALID_ARGUMENT, "fe_layernorm_dual: null pointer");
+    return done(fe::launch_layernorm_dual(x, gamma, beta, h32, h16, rows, dim, eps,
+                                          reinterpret_cast<cudaStream_t>(stream)),
+                "fe_layernorm_dual");
+}
+
+fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, int32_t dim, fe_pooling mode,
+                     float *out, fe_stream_t stream)
+{
+    if (batch < 0 || dim <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_pool_l2: bad shape");
+    if (mode != FE_POOL_CLS && mode != FE_POOL_MEAN && mode != FE_POOL_LAST)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_pool_l2: unknown pooling mode");
+    if (batch == 0) return FE_OK;
+    if (!h || !cu_seqlens || !out) return fail(FE_ERR_INVALID_ARGUMENT, "fe_pool_l2: null pointer");
+    return done(fe::launch_pool_l2(h, cu_seqlens, batch, dim, mode, out, reinterpret_cast<cudaStream_t>(stream)),
+                "fe_pool_l2");
+}
+
+// ------------------------------------------------------------ host-only helpers
+fe_status fe_plan_shards(const fe_encoder_config *cfg, const int32_t *sorted_lengths, int32_t batch, int32_t parts,
+                         int32_t *cuts)
+{
+    if (!cfg || batch < 0 || parts < 1 || (batch && !sorted_lengths) || (parts > 1 && !cuts))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_plan_shards: bad arguments");
+    const double D = cfg->hidden, F = cfg->intermediate;
+    std::vector<double> prefix(static_cast<size_t>(batch) + 1, 0.0);
+    for (int32_t i = 0; i < batch; ++i) {
+        const double L = sorted_lengths[i];
+        if (i && sorted_lengths[i] > sorted_lengths[i - 1])
+            return fail(FE_ERR_INVALID_ARGUMENT, "fe_plan_shards: lengths must be sorted in descending order");
+        prefix[i + 1] = prefix[i] + cfg->layers * (2.0 * L * (4 * D * D + 2 * D * F) + 4.0 * L * L * D);
+    }
+    const double total = prefix[batch];
+    int32_t lo = 0;
+    for (int32_t r = 1; r < parts; ++r) {
+        const double target = total * r / parts;
+        int32_t i = static_cast<int32_t>(std::lower_bound(prefix.begin(), prefix.end(), target) - prefix.begin());
+        if (i > 0 && (i > batch || target - prefix[i - 1] <= prefix[i] - target)) --i;
+        i = std::min(std::max(i, lo), batch);
+        cuts[r - 1] = i;
+        lo = i;
+    }
+    return FE_OK;
+}
+
+fe_status fe_pack_batch(const int32_t *ids, const int32_t *lengths, int32_t batch, int32_t stride,
+                        int32_t *ids_packed, int32_t *cu_seqlens)
+{
+    if (batch < 0 || stride < 0 || (batch && (!ids || !lengths || !cu_seqlens)))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_pack_batch: bad arguments");
+    int64_t off = 0;
+    if (cu_seqlens) cu_seqlens[0] = 0;
+    for (int32_t b = 0; b < batch; ++b) {
+        const int32_t L = lengths[b];
+        if (L < 0 || L > stride) return fail(FE_ERR_INVALID_ARGUMENT, "fe_pack_batch: length outside [0, stride]");
+        if (off + L > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_pack_batch: too many tokens");
+        if (L && !ids_packed) return fail(FE_ERR_INVALID_ARGUMENT, "fe_pack_batch: null output");
+        std::copy(ids + static_cast<int64_t>(b) * stride, ids + static_cast<int64_t>(b) * stride + L, ids_packed + off);
+        off += L;
+        cu_seqlens[b + 1] = static_cast<int32_t>(off);
+    }
+    return FE_OK;
+}
+
+}  // extern "C"

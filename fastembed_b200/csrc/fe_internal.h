@@ -1,0 +1,78 @@
+// fe_internal.h — host-side declarations shared by the library's translation units:
+// error reporting, the per-device status word, TMA descriptor encoding and the
+// kernel launchers behind the C ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "fastembed_b200.h"
+
+namespace fe {
+
+// Codes kernels write into the per-device status word.
+enum : int { DEV_OK = 0, DEV_BAD_INPUT = 1, DEV_TIMEOUT = 5 };
+
+// Records `msg` as this thread's last error and returns `s`.
+fe_status fail(fe_status s, const std::string &msg);
+// Maps a CUDA error to a status (recording its text); cudaSuccess -> FE_OK.
+fe_status check_cuda(cudaError_t err, const char *what);
+
+#define FE_TRY_CUDA(expr)                                             \
+    do {                                                              \
+        cudaError_t fe_err_ = (expr);                                 \
+        if (fe_err_ != cudaSuccess) return ::fe::check_cuda(fe_err_, #expr); \
+    } while (0)
+
+#define FE_TRY(expr)                          \
+    do {                                      \
+        fe_status fe_st_ = (expr);            \
+        if (fe_st_ != FE_OK) return fe_st_;   \
+    } while (0)
+
+// Per-device int32 status word that kernels write on bounded-wait timeout or bad
+// input (allocated once per device on first use).
+int *device_status_word(int device);
+int *current_device_status_word();
+int current_sm_count();
+
+// TMA descriptor for a row-major 2-D tensor [rows, cols] of `elem_bytes` elements
+// with row stride `ld` elements, box [box_rows, box_cols], 128B swizzle unless
+// swizzle128 is false.
+fe_status make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype,
+                       int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld,
+                       uint32_t box_rows, uint32_t box_cols, bool swizzle128 = true);
+
+// ---- launchers (no argument validation; the C ABI validates) ----
+cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
+                               const float *residual, void *y, int64_t m, int64_t n, int64_t k,
+                               int epilogue, int y_dtype, cudaStream_t s, fe_status *st);
+cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, int batch,
+                                    int max_len, int heads, int head_dim, void *out,
+                                    int64_t total_tokens, cudaStream_t s, fe_status *st);
+cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
+                                   const float *word, const float *pos, const float *type,
+                                   const float *g, const float *b, int dim, int vocab,
+                                   int max_pos, float eps, float *h32, void *h16, cudaStream_t s);
+cudaError_t launch_layernorm_dual(const float *x, const float *g, const float *b, float *h32,
+                                  void *h16, int64_t rows, int dim, float eps, cudaStream_t s);
+cudaError_t launch_pool_l2(const float *h, const int32_t *cu, int batch, int dim, int mode,
+                           float *out, cudaStream_t s);
+cudaError_t launch_f32_to_bf16(const float *x, void *y, int64_t count, cudaStream_t s);
+
+cudaError_t launch_sgemm(const float *a, const float *b, const float *bias, float *c, int64_t m,
+                         int64_t n, int64_t k, bool b_transposed, cudaStream_t s);
+cudaError_t launch_unary(int op, const float *x, float *y, int64_t count, cudaStream_t s);
+cudaError_t launch_layer_norm_f32(const float *x, const float *g, const float *b, float *y,
+                                  int64_t rows, int64_t dim, float eps, cudaStream_t s);
+cudaError_t launch_rms_norm_f32(const float *x, const float *w, float *y, int64_t rows,
+                                int64_t dim, float eps, cudaStream_t s);
+cudaError_t launch_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t dim,
+                                    cudaStream_t s);
+cudaError_t launch_mha_core_f32(const float *q, const float *k, const float *v, float *out,
+                                int64_t seq_len, int64_t dim, int64_t heads, cudaStream_t s);
+
+}  // namespace fe

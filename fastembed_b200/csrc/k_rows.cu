@@ -1,0 +1,326 @@
+// k_rows.cu — memory-bound row kernels of the encoder pipeline: fused embedding
+// sum + LayerNorm, LayerNorm with fp32 + bf16 outputs, pooling + L2 normalise, and
+// the fp32 -> bf16 weight conversion.  All are HBM-bound: one warp per row, float4
+// loads, two-pass statistics held in registers, warp-shuffle reductions.
+#include <cuda_bf16.h>
+
+#include "fe_common.cuh"
+#include "fe_internal.h"
+
+namespace fe {
+namespace {
+
+// Row LayerNorm of VPT float4 per lane (dim = 128 * VPT), values already in
+// registers; writes fp32 and (optionally) bf16.  Two-pass mean / variance as in
+// src/ops/cpu/cpu_matrix_ops.cpp:64-92, normalised with a true division.
+template <int VPT>
+__device__ __forceinline__ void ln_store(float4 (&x)[VPT], const float *__restrict__ g,
+                                         const float *__restrict__ b, float *__restrict__ y32,
+                                         __nv_bfloat16 *__restrict__ y16, int dim, float eps, int lane)
+{
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) s += (x[i].x + x[i].y) + (x[i].z + x[i].w);
+    const float mean = warp_sum(s) / static_cast<float>(dim);
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const float a = x[i].x - mean, bb = x[i].y - mean, c = x[i].z - mean, d = x[i].w - mean;
+        v += (a * a + bb * bb) + (c * c + d * d);
+    }
+    const float var = warp_sum(v) / static_cast<float>(dim);
+    const float sd = sqrtf(var + eps);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int col = (i * 32 + lane) * 4;
+        const float4 gg = __ldg(reinterpret_cast<const float4 *>(g + col));
+        const float4 bv = __ldg(reinterpret_cast<const float4 *>(b + col));
+        float4 o;
+        o.x = (x[i].x - mean) / sd * gg.x + bv.x;
+        o.y = (x[i].y - mean) / sd * gg.y + bv.y;
+        o.z = (x[i].z - mean) / sd * gg.z + bv.z;
+        o.w = (x[i].w - mean) / sd * gg.w + bv.w;
+        *reinterpret_cast<float4 *>(y32 + col) = o;
+        if (y16) {
+            uint2 p;
+            p.x = pack_bf16x2(o.x, o.y);
+            p.y = pack_bf16x2(o.z, o.w);
+            *reinterpret_cast<uint2 *>(y16 + col) = p;
+        }
+    }
+}
+
+// Token t of sentence s: x = word[id] + pos[t - start(s)] + type[0] (summed in that
+// order, src/sentence_transformers_impl.cpp:30-44, :155-188), then LayerNorm (:189-194).
+template <int VPT>
+__global__ void __launch_bounds__(256)
+    embed_ln(const int32_t *__restrict__ ids, const int32_t *__restrict__ cu, int batch, int64_t total,
+             const float *__restrict__ word, const float *__restrict__ pos, const float *__restrict__ type,
+             const float *__restrict__ g, const float *__restrict__ b, int vocab, int max_pos, float eps,
+             float *__restrict__ h32, __nv_bfloat16 *__restrict__ h16, int *status)
+{
+    constexpr int dim = 128 * VPT;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= total) return;
+    // sentence of token t: last s with cu[s] <= t
+    int lo = 0, hi = batch - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    const int p = static_cast<int>(t - cu[lo]);
+    const int id = ids[t];
+    float *o32 = h32 + t * dim;
+    __nv_bfloat16 *o16 = h16 ? h16 + t * dim : nullptr;
+    if (id < 0 || id >= vocab || p < 0 || p >= max_pos) {
+        if (lane == 0) report(status, DEV_BAD_INPUT);
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int col = (i * 32 + lane) * 4;
+            *reinterpret_cast<float4 *>(o32 + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (o16) *reinterpret_cast<uint2 *>(o16 + col) = make_uint2(0u, 0u);
+        }
+        return;
+    }
+    const float *wr = word + static_cast<int64_t>(id) * dim;
+    const float *pr = pos + static_cast<int64_t>(p) * dim;
+    float4 x[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int col = (i * 32 + lane) * 4;
+        const float4 a = __ldg(reinterpret_cast<const float4 *>(wr + col));
+        const float4 c = __ldg(reinterpret_cast<const float4 *>(pr + col));
+        const float4 d = __ldg(reinterpret_cast<const float4 *>(type + col));
+        x[i] = make_float4((a.x + c.x) + d.x, (a.y + c.y) + d.y, (a.z + c.z) + d.z, (a.w + c.w) + d.w);
+    }
+    ln_store<VPT>(x, g, b, o32, o16, dim, eps, lane);
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(256)
+    ln_dual(const float *__restrict__ in, const float *__restrict__ g, const float *__restrict__ b,
+            float *__restrict__ h32, __nv_bfloat16 *__restrict__ h16, int64_t rows, float eps)
+{
+    constexpr int dim = 128 * VPT;
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const float *src = in + r * dim;
+    float4 x[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) x[i] = *reinterpret_cast<const float4 *>(src + (i * 32 + lane) * 4);
+    ln_store<VPT>(x, g, b, h32 + r * dim, h16 ? h16 + r * dim : nullptr, dim, eps, lane);
+}
+
+// Generic-width LayerNorm (any dim): one block per row, block reductions.
+__device__ float block_sum(float v, float *red)
+{
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    if (w == 0) t = warp_sum(t);
+    if (threadIdx.x == 0) red[32] = t;
+    __syncthreads();
+    return red[32];
+}
+
+__device__ float block_max(float v, float *red)
+{
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
+    if (w == 0) t = warp_max(t);
+    if (threadIdx.x == 0) red[32] = t;
+    __syncthreads();
+    return red[32];
+}
+
+__global__ void __launch_bounds__(256)
+    ln_generic(const float *__restrict__ in, const float *__restrict__ g, const float *__restrict__ b,
+               float *__restrict__ h32, __nv_bfloat16 *__restrict__ h16, int64_t dim, float eps)
+{
+    __shared__ float red[33];
+    const float *x = in + static_cast<int64_t>(blockIdx.x) * dim;
+    float s = 0.f;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) s += x[i];
+    const float mean = block_sum(s, red) / static_cast<float>(dim);
+    float v = 0.f;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float d = x[i] - mean;
+        v += d * d;
+    }
+    const float var = block_sum(v, red) / static_cast<float>(dim);
+    const float sd = sqrtf(var + eps);
+    float *y = h32 + static_cast<int64_t>(blockIdx.x) * dim;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float o = (x[i] - mean) / sd * g[i] + b[i];
+        y[i] = o;
+        if (h16) h16[static_cast<int64_t>(blockIdx.x) * dim + i] = __float2bfloat16_rn(o);
+    }
+}
+
+// RMSNorm, src/ops/cpu/cpu_matrix_ops.cpp:95-121: inv = 1/sqrt(mean(x^2)+eps); y = inv*w*x.
+__global__ void __launch_bounds__(256)
+    rms_generic(const float *__restrict__ in, const float *__restrict__ w, float *__restrict__ out,
+                int64_t dim, float eps)
+{
+    __shared__ float red[33];
+    const float *x = in + static_cast<int64_t>(blockIdx.x) * dim;
+    float s = 0.f;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) s += x[i] * x[i];
+    float ms = block_sum(s, red) / static_cast<float>(dim);
+    const float inv = 1.0f / sqrtf(ms + eps);
+    float *y = out + static_cast<int64_t>(blockIdx.x) * dim;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) y[i] = inv * w[i] * x[i];
+}
+
+// Row softmax, src/ops/cpu/cpu_matrix_ops.cpp:141-163 (in == out allowed).
+__global__ void __launch_bounds__(256)
+    softmax_generic(const float *in, float *out, int64_t dim)
+{
+    __shared__ float red[33];
+    const float *x = in + static_cast<int64_t>(blockIdx.x) * dim;
+    float *y = out + static_cast<int64_t>(blockIdx.x) * dim;
+    float m = -INFINITY;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) m = fmaxf(m, x[i]);
+    m = block_max(m, red);
+    float s = 0.f;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float e = expf(x[i] - m);
+        y[i] = e;
+        s += e;
+    }
+    s = block_sum(s, red);
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) y[i] = y[i] / s;
+}
+
+// Pooling + L2 (src/sentence_transformers_impl.cpp:289-341): one warp per sentence.
+__global__ void __launch_bounds__(256)
+    pool_l2(const float *__restrict__ h, const int32_t *__restrict__ cu, int batch, int dim, int mode,
+            float *__restrict__ out)
+{
+    const int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (s >= batch) return;
+    const int start = cu[s], len = cu[s + 1] - cu[s];
+    float *o = out + static_cast<int64_t>(s) * dim;
+    if (len <= 0) {
+        for (int c = lane; c < dim; c += 32) o[c] = 0.f;
+        return;
+    }
+    float ss = 0.f;
+    if (mode == FE_POOL_MEAN) {
+        for (int c = lane; c < dim; c += 32) {
+            float acc = 0.f;
+            for (int t = 0; t < len; ++t) acc += h[static_cast<int64_t>(start + t) * dim + c];
+            acc /= static_cast<float>(len);
+            o[c] = acc;
+            ss += acc * acc;
+        }
+    } else {
+        const int row = mode == FE_POOL_LAST ? start + len - 1 : start;
+        const float *src = h + static_cast<int64_t>(row) * dim;
+        for (int c = lane; c < dim; c += 32) {
+            const float v = src[c];
+            o[c] = v;
+            ss += v * v;
+        }
+    }
+    const float nrm = sqrtf(warp_sum(ss));
+    for (int c = lane; c < dim; c += 32) o[c] = o[c] / nrm;
+}
+
+__global__ void f32_to_bf16(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y, int64_t n)
+{
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+
+inline unsigned grid_for(int64_t rows, int per_block) { return static_cast<unsigned>((rows + per_block - 1) / per_block); }
+
+}  // namespace
+
+cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
+                                   const float *word, const float *pos, const float *type,
+                                   const float *g, const float *b, int dim, int vocab, int max_pos,
+                                   float eps, float *h32, void *h16, cudaStream_t s)
+{
+    if (total == 0) return cudaSuccess;
+    auto *o16 = static_cast<__nv_bfloat16 *>(h16);
+    int *st = current_device_status_word();
+    const unsigned grid = grid_for(total, 8);
+    switch (dim) {
+#define FE_EMB(V) \
+    case 128 * V: embed_ln<V><<<grid, 256, 0, s>>>(ids, cu, batch, total, word, pos, type, g, b, vocab, max_pos, eps, h32, o16, st); break;
+        FE_EMB(2) FE_EMB(3) FE_EMB(4) FE_EMB(6) FE_EMB(8) FE_EMB(12) FE_EMB(16)
+#undef FE_EMB
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_dual(const float *x, const float *g, const float *b, float *h32, void *h16,
+                                  int64_t rows, int dim, float eps, cudaStream_t s)
+{
+    if (rows == 0) return cudaSuccess;
+    auto *o16 = static_cast<__nv_bfloat16 *>(h16);
+    const unsigned grid = grid_for(rows, 8);
+    switch (dim) {
+#define FE_LN(V) \
+    case 128 * V: ln_dual<V><<<grid, 256, 0, s>>>(x, g, b, h32, o16, rows, eps); break;
+        FE_LN(1) FE_LN(2) FE_LN(3) FE_LN(4) FE_LN(6) FE_LN(8) FE_LN(12) FE_LN(16)
+#undef FE_LN
+        default: ln_generic<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, g, b, h32, o16, dim, eps);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layer_norm_f32(const float *x, const float *g, const float *b, float *y, int64_t rows,
+                                  int64_t dim, float eps, cudaStream_t s)
+{
+    if (rows == 0) return cudaSuccess;
+    ln_generic<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, g, b, y, nullptr, dim, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm_f32(const float *x, const float *w, float *y, int64_t rows, int64_t dim,
+                                float eps, cudaStream_t s)
+{
+    if (rows == 0) return cudaSuccess;
+    rms_generic<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, w, y, dim, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t dim, cudaStream_t s)
+{
+    if (rows == 0) return cudaSuccess;
+    softmax_generic<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, y, dim);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pool_l2(const float *h, const int32_t *cu, int batch, int dim, int mode, float *out,
+                           cudaStream_t s)
+{
+    if (batch == 0) return cudaSuccess;
+    pool_l2<<<grid_for(batch, 8), 256, 0, s>>>(h, cu, batch, dim, mode, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_bf16(const float *x, void *y, int64_t count, cudaStream_t s)
+{
+    if (count == 0) return cudaSuccess;
+    int64_t blocks = (count + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    f32_to_bf16<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, static_cast<__nv_bfloat16 *>(y), count);
+    return cudaGetLastError();
+}
+
+}  // namespace fe

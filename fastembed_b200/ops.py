@@ -1,0 +1,236 @@
+"""Torch-tensor front end of the C ABI: each function checks shapes, passes raw
+device pointers and the current torch stream to libfastembed_b200.so, and raises
+FeError on a non-OK status.  PyTorch only supplies device memory and streams."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import capi
+from .capi import ACT, DTYPE, EPI, POOL, call
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _s(t: torch.Tensor):
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise ValueError("expected contiguous CUDA tensors")
+
+
+# ---------------------------------------------------------------- fp32 op API
+def sgemm_nn(a, b, m, n, k):
+    _cuda(a, b)
+    c = torch.empty(m * k, dtype=torch.float32, device=a.device)
+    call("fe_sgemm_nn", _p(a), _p(b), _p(c), m, n, k, _s(a))
+    return c
+
+
+def sgemm_nt(a, b, m, n, k, bias=None):
+    _cuda(a, b, bias)
+    c = torch.empty(m * k, dtype=torch.float32, device=a.device)
+    call("fe_sgemm_nt", _p(a), _p(b), _p(bias), _p(c), m, n, k, _s(a))
+    return c
+
+
+def unary(name, x):
+    _cuda(x)
+    y = torch.empty_like(x)
+    call(f"fe_{name}_f32", _p(x), _p(y), x.numel(), _s(x))
+    return y
+
+
+def layer_norm_f32(x, g, b, dim, eps):
+    _cuda(x, g, b)
+    y = torch.empty_like(x)
+    call("fe_layer_norm_f32", _p(x), _p(g), _p(b), _p(y), x.numel() // dim, dim, eps, _s(x))
+    return y
+
+
+def rms_norm_f32(x, w, dim, eps):
+    _cuda(x, w)
+    y = torch.empty_like(x)
+    call("fe_rms_norm_f32", _p(x), _p(w), _p(y), x.numel() // dim, dim, eps, _s(x))
+    return y
+
+
+def softmax_rows_f32(x, dim):
+    _cuda(x)
+    y = torch.empty_like(x)
+    call("fe_softmax_rows_f32", _p(x), _p(y), x.numel() // dim, dim, _s(x))
+    return y
+
+
+def softmax_scores_inplace(scores, heads, seq_len):
+    _cuda(scores)
+    call("fe_softmax_scores_inplace_f32", _p(scores), heads, seq_len, _s(scores))
+    return scores
+
+
+def mha_f32(x, wq, wk, wv, bq, bk, bv, heads, dim):
+    _cuda(x, wq, wk, wv, bq, bk, bv)
+    L = x.numel() // dim
+    out = torch.empty(L * dim, dtype=torch.float32, device=x.device)
+    nbytes = capi.lib().fe_mha_f32_workspace_bytes(L, dim, heads)
+    ws = torch.empty(max(nbytes, 4), dtype=torch.uint8, device=x.device)
+    call("fe_mha_f32", _p(x), _p(wq), _p(wk), _p(wv), _p(bq), _p(bk), _p(bv), _p(out), L, dim, heads,
+         _p(ws), nbytes, _s(x))
+    return out
+
+
+# ---------------------------------------------------------- bf16 hot-path ops
+def linear_bf16(x, w, bias=None, residual=None, epilogue="none", out_dtype="bf16"):
+    """y = epilogue(x @ w.T): x [m,k] bf16, w [n,k] bf16."""
+    _cuda(x, w, bias, residual)
+    m, k = x.shape
+    n = w.shape[0]
+    y = torch.empty(m, n, dtype=torch.bfloat16 if out_dtype == "bf16" else torch.float32, device=x.device)
+    call("fe_linear_bf16", _p(x), _p(w), _p(bias), _p(residual), _p(y), m, n, k, EPI[epilogue],
+         DTYPE[out_dtype], _s(x))
+    return y
+
+
+def attention_varlen(qkv, cu_seqlens, max_len, heads, head_dim=64):
+    _cuda(qkv, cu_seqlens)
+    T = qkv.shape[0]
+    out = torch.empty(T, heads * head_dim, dtype=torch.bfloat16, device=qkv.device)
+    call("fe_attention_varlen_bf16", _p(qkv), _p(cu_seqlens), cu_seqlens.numel() - 1, max_len, heads, head_dim,
+         _p(out), T, _s(qkv))
+    return out
+
+
+def embed_layernorm(ids, cu_seqlens, word, pos, type_, gamma, beta, eps):
+    _cuda(ids, cu_seqlens, word, pos, type_, gamma, beta)
+    T = ids.numel()
+    D = word.shape[1]
+    h32 = torch.empty(T, D, dtype=torch.float32, device=ids.device)
+    h16 = torch.empty(T, D, dtype=torch.bfloat16, device=ids.device)
+    call("fe_embed_layernorm", _p(ids), _p(cu_seqlens), cu_seqlens.numel() - 1, T, _p(word), _p(pos), _p(type_),
+         _p(gamma), _p(beta), D, word.shape[0], pos.shape[0], eps, _p(h32), _p(h16), _s(ids))
+    return h32, h16
+
+
+def layernorm_dual(x, gamma, beta, eps):
+    _cuda(x, gamma, beta)
+    rows, D = x.shape
+    h32 = torch.empty_like(x)
+    h16 = torch.empty(rows, D, dtype=torch.bfloat16, device=x.device)
+    call("fe_layernorm_dual", _p(x), _p(gamma), _p(beta), _p(h32), _p(h16), rows, D, eps, _s(x))
+    return h32, h16
+
+
+def pool_l2(h, cu_seqlens, mode="cls"):
+    _cuda(h, cu_seqlens)
+    B = cu_seqlens.numel() - 1
+    D = h.shape[1]
+    out = torch.empty(B, D, dtype=torch.float32, device=h.device)
+    call("fe_pool_l2", _p(h), _p(cu_seqlens), B, D, POOL[mode], _p(out), _s(h))
+    return out
+
+
+def device_status(device: int = 0) -> None:
+    capi.check(capi.lib().fe_device_status(device), "fe_device_status")
+
+
+# ------------------------------------------------------------------- engine
+class Engine:
+    """One device-resident encoder (fe_engine) on one GPU."""
+
+    def __init__(self, shape, device: int = 0, pooling: str = "cls"):
+        self.shape = shape
+        self.device = device
+        cfg = capi.EncoderConfig(shape.vocab, shape.hidden, shape.layers, shape.heads, shape.intermediate,
+                                 shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], POOL[pooling])
+        self._cfg = cfg
+        h = C.c_void_p()
+        capi.check(capi.lib().fe_engine_create(C.byref(cfg), device, C.byref(h)), "fe_engine_create")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            capi.lib().fe_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_weight(self, name: str, value) -> None:
+        if isinstance(value, torch.Tensor) and value.is_cuda:
+            v = value.contiguous().float()
+            call("fe_engine_set_weight", self.h, name.encode(), _p(v), v.numel(), 1)
+        else:
+            v = np.ascontiguousarray(value, dtype=np.float32)
+            call("fe_engine_set_weight", self.h, name.encode(), v.ctypes.data_as(C.c_void_p), v.size, 0)
+
+    def load_weights(self, weights: dict) -> None:
+        for name, v in weights.items():
+            if name.startswith("pooler."):
+                continue  # read but unused by the reference forward (sentence_transformers_impl.cpp:285-331)
+            self.set_weight(name, v)
+        missing = capi.lib().fe_engine_missing_weights(self.h)
+        if missing:
+            raise ValueError(f"{missing} weights missing")
+
+    def load_safetensors(self, path: str) -> None:
+        call("fe_engine_load_safetensors", self.h, path.encode())
+
+    def encode_host(self, ids: np.ndarray, lengths: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        lengths = np.ascontiguousarray(lengths, dtype=np.int32)
+        B, S = ids.shape
+        out = np.empty((B, self.shape.hidden), np.float32)
+        call("fe_engine_encode_host", self.h, ids.ctypes.data_as(C.c_void_p), lengths.ctypes.data_as(C.c_void_p),
+             B, S, out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def encode_packed(self, ids_dev: torch.Tensor, cu_dev: torch.Tensor, cu_host: np.ndarray,
+                      out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        cu_host = np.ascontiguousarray(cu_host, dtype=np.int32)
+        B = cu_host.size - 1
+        if out is None:
+            out = torch.empty(B, self.shape.hidden, dtype=torch.float32, device=ids_dev.device)
+        st = stream if stream is not None else torch.cuda.current_stream(ids_dev.device)
+        call("fe_engine_encode_packed", self.h, _p(ids_dev), _p(cu_dev), cu_host.ctypes.data_as(C.c_void_p), B,
+             _p(out), C.c_void_p(st.cuda_stream))
+        return out
+
+    def set_profiling(self, on: bool) -> None:
+        call("fe_engine_set_profiling", self.h, 1 if on else 0)
+
+    def stats(self) -> dict:
+        s = capi.EngineStats()
+        call("fe_engine_get_stats", self.h, C.byref(s))
+        return {k: getattr(s, k) for k, _ in s._fields_}
+
+
+def pack(ids: np.ndarray, lengths: np.ndarray):
+    """Host packing through the library's fe_pack_batch: (ids_packed, cu_seqlens)."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    lengths = np.ascontiguousarray(lengths, dtype=np.int32)
+    B, S = ids.shape
+    packed = np.empty(max(int(lengths.sum()), 1), np.int32)
+    cu = np.empty(B + 1, np.int32)
+    call("fe_pack_batch", ids.ctypes.data_as(C.c_void_p), lengths.ctypes.data_as(C.c_void_p), B, S,
+         packed.ctypes.data_as(C.c_void_p), cu.ctypes.data_as(C.c_void_p))
+    return packed[:int(lengths.sum())], cu
+
+
+def plan_shards(shape, sorted_lengths: np.ndarray, parts: int) -> list[int]:
+    cfg = capi.EncoderConfig(shape.vocab, shape.hidden, shape.layers, shape.heads, shape.intermediate,
+                             shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], 0)
+    L = np.ascontiguousarray(sorted_lengths, dtype=np.int32)
+    cuts = np.zeros(max(parts - 1, 1), np.int32)
+    call("fe_plan_shards", C.byref(cfg), L.ctypes.data_as(C.c_void_p), L.size, parts,
+         cuts.ctypes.data_as(C.c_void_p))
+    return [int(c) for c in cuts[:parts - 1]]

@@ -1,0 +1,198 @@
+"""Synthetic encoder workloads: model shapes, sentence lengths, token ids, weights.
+
+The reference publishes no dataset or checkpoint for its benchmarks, so every
+workload is synthetic and seeded:
+
+* weights ~ N(0, 0.02) (seed 0), LayerNorm gamma = 1, beta = 0, biases N(0, 0.02),
+  named exactly as the reference reads them from model.safetensors
+  (src/sentence_transformers_impl.cpp:33, :132, :171, :192-193, :201-218, :285-286);
+* token ids uniform in [100, vocab) with [CLS]=101 first and [SEP]=102 last, the
+  framing the reference's tokenize() adds (src/sentence_transformers_impl.cpp:21-22);
+  input seed 1;
+* sentence lengths per shape below; sentences run unpadded (packed) on the device.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+
+CLS_ID = 101
+SEP_ID = 102
+PAD_ID = 0
+
+
+@dataclasses.dataclass(frozen=True)
+class EncoderShape:
+    name: str
+    layers: int
+    hidden: int
+    heads: int
+    intermediate: int
+    vocab: int = 21128
+    max_pos: int = 512
+    type_vocab: int = 2
+    eps: float = 1e-12
+    act: str = "gelu"
+    batch: int = 8
+    lengths: tuple = ("uniform", 16, 128)
+    pad_to: int = 128
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+    def flops_per_sentence(self, length: int) -> float:
+        """Algorithmic FLOPs of one unpadded sentence:
+        layers * [2 L (4 D^2 + 2 D F) + 4 L^2 D] (projections + QK^T + PV)."""
+        D, F, L = self.hidden, self.intermediate, length
+        return self.layers * (2.0 * L * (4 * D * D + 2 * D * F) + 4.0 * L * L * D)
+
+    def gemm_flops_per_sentence(self, length: int) -> float:
+        D, F, L = self.hidden, self.intermediate, length
+        return self.layers * 2.0 * L * (4 * D * D + 2 * D * F)
+
+    def attn_flops_per_sentence(self, length: int) -> float:
+        return self.layers * 4.0 * length * length * self.hidden
+
+
+SHAPES = {
+    # BGE-small-zh shape: 4 layers, D 512, 8 heads, FFN 2048; batch 8, L ~ U[16,128]
+    "bge-small": EncoderShape("bge-small", 4, 512, 8, 2048, batch=8,
+                              lengths=("uniform", 16, 128), pad_to=128),
+    # BGE-base-zh shape: 12 layers, D 768, 12 heads, FFN 3072; batch 64, L ~ U[32,512]
+    "bge-base": EncoderShape("bge-base", 12, 768, 12, 3072, batch=64,
+                             lengths=("uniform", 32, 512), pad_to=512),
+    # BGE-large-zh shape: 24 layers, D 1024, 16 heads, FFN 4096; batch 256,
+    # L ~ lognormal(median 96, sigma 0.6) truncated to [8, 512]
+    "bge-large": EncoderShape("bge-large", 24, 1024, 16, 4096, batch=256,
+                              lengths=("lognormal", 96, 0.6, 8, 512), pad_to=512),
+}
+
+
+def sample_lengths(shape: EncoderShape, batch: int | None = None, seed: int = 1) -> np.ndarray:
+    """Sentence lengths (including [CLS] and [SEP]) for `batch` sentences."""
+    rng = np.random.default_rng(seed)
+    b = shape.batch if batch is None else batch
+    kind = shape.lengths[0]
+    if kind == "uniform":
+        lo, hi = shape.lengths[1], shape.lengths[2]
+        return rng.integers(lo, hi + 1, size=b).astype(np.int32)
+    if kind == "lognormal":
+        median, sigma, lo, hi = shape.lengths[1:]
+        out = np.empty(b, dtype=np.int32)
+        n = 0
+        while n < b:  # rejection-truncate to [lo, hi]
+            v = np.round(rng.lognormal(math.log(median), sigma, size=2 * b)).astype(np.int64)
+            v = v[(v >= lo) & (v <= hi)]
+            take = min(b - n, v.size)
+            out[n:n + take] = v[:take]
+            n += take
+        return out
+    raise ValueError(f"unknown length distribution {kind!r}")
+
+
+def sample_ids(shape: EncoderShape, lengths: np.ndarray, seed: int = 1, pad_to: int | None = None):
+    """Right-padded ids [B, S] (PAD=0) and the matching 1/0 attention mask."""
+    rng = np.random.default_rng(seed + 1000)
+    S = int(max(pad_to or shape.pad_to, int(lengths.max()) if lengths.size else 1))
+    B = lengths.size
+    ids = np.zeros((B, S), dtype=np.int32)
+    mask = np.zeros((B, S), dtype=np.int32)
+    for b, L in enumerate(lengths):
+        L = int(L)
+        row = rng.integers(100, shape.vocab, size=L, dtype=np.int64).astype(np.int32)
+        row[0] = CLS_ID
+        if L > 1:
+            row[L - 1] = SEP_ID
+        ids[b, :L] = row
+        mask[b, :L] = 1
+    return ids, mask
+
+
+def weight_names(shape: EncoderShape) -> list[tuple[str, tuple[int, ...], str]]:
+    """(HF name, shape, init) for every tensor the encoder reads, in a fixed order."""
+    D, F = shape.hidden, shape.intermediate
+    out = [
+        ("embeddings.word_embeddings.weight", (shape.vocab, D), "normal"),
+        ("embeddings.position_embeddings.weight", (shape.max_pos, D), "normal"),
+        ("embeddings.token_type_embeddings.weight", (shape.type_vocab, D), "normal"),
+        ("embeddings.LayerNorm.weight", (D,), "ones"),
+        ("embeddings.LayerNorm.bias", (D,), "zeros"),
+    ]
+    for l in range(shape.layers):
+        p = f"encoder.layer.{l}."
+        out += [
+            (p + "attention.self.query.weight", (D, D), "normal"),
+            (p + "attention.self.query.bias", (D,), "normal"),
+            (p + "attention.self.key.weight", (D, D), "normal"),
+            (p + "attention.self.key.bias", (D,), "normal"),
+            (p + "attention.self.value.weight", (D, D), "normal"),
+            (p + "attention.self.value.bias", (D,), "normal"),
+            (p + "attention.output.dense.weight", (D, D), "normal"),
+            (p + "attention.output.dense.bias", (D,), "normal"),
+            (p + "attention.output.LayerNorm.weight", (D,), "ones"),
+            (p + "attention.output.LayerNorm.bias", (D,), "zeros"),
+            (p + "intermediate.dense.weight", (F, D), "normal"),
+            (p + "intermediate.dense.bias", (F,), "normal"),
+            (p + "output.dense.weight", (D, F), "normal"),
+            (p + "output.dense.bias", (D,), "normal"),
+            (p + "output.LayerNorm.weight", (D,), "ones"),
+            (p + "output.LayerNorm.bias", (D,), "zeros"),
+        ]
+    out += [("pooler.dense.weight", (D, D), "normal"), ("pooler.dense.bias", (D,), "normal")]
+    return out
+
+
+def make_weights(shape: EncoderShape, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
+    """Seeded random-init FP32 weights, keyed by HF tensor name."""
+    rng = np.random.default_rng(seed)
+    w: dict[str, np.ndarray] = {}
+    for name, shp, init in weight_names(shape):
+        if init == "normal":
+            a = rng.standard_normal(size=shp, dtype=np.float32)
+            a *= np.float32(std)
+        elif init == "ones":
+            a = np.ones(shp, dtype=np.float32)
+        else:
+            a = np.zeros(shp, dtype=np.float32)
+        w[name] = a
+    return w
+
+
+def config_json(shape: EncoderShape) -> dict:
+    """The config.json keys the reference reads (src/sentence_transformers_impl.cpp:47-98,
+    :189, :199, :240, :268, :413)."""
+    return {
+        "model_type": "bert",
+        "vocab_size": shape.vocab,
+        "hidden_size": shape.hidden,
+        "num_hidden_layers": shape.layers,
+        "num_attention_heads": shape.heads,
+        "intermediate_size": shape.intermediate,
+        "hidden_act": shape.act,
+        "layer_norm_eps": shape.eps,
+        "max_position_embeddings": shape.max_pos,
+        "type_vocab_size": shape.type_vocab,
+        "pad_token_id": 0,
+    }
+
+
+def balanced_cuts(shape: EncoderShape, sorted_lengths: np.ndarray, parts: int) -> list[int]:
+    """Contiguous cut points of a length-sorted batch into `parts` slices whose
+    algorithmic FLOPs are as equal as a greedy prefix cut gets them."""
+    if parts <= 1:
+        return []
+    w = np.array([shape.flops_per_sentence(int(L)) for L in sorted_lengths], dtype=np.float64)
+    prefix = np.concatenate([[0.0], np.cumsum(w)])  # prefix[i] = work of the first i sentences
+    total = prefix[-1]
+    cuts: list[int] = []
+    for r in range(1, parts):
+        target = total * r / parts
+        i = int(np.searchsorted(prefix, target))  # prefix[i-1] < target <= prefix[i]
+        if i > 0 and (i >= prefix.size or target - prefix[i - 1] <= prefix[i] - target):
+            i -= 1
+        lo = cuts[-1] if cuts else 0
+        cuts.append(int(min(max(i, lo), sorted_lengths.size)))
+    return cuts

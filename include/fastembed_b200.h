@@ -1,0 +1,231 @@
+/*
+ * fastembed_b200.h — C ABI of the B200 (sm_100a) encoder forward path.
+ *
+ * Drop-in boundary for fastEmbed's op classes and model runtime.  The reference
+ * has no C ABI: its boundary is the C++ classes CUDAMatrixOps
+ * (include/ops/cuda/cuda_matrix_ops.h:4-45), CUDAAttentionOps
+ * (include/ops/cuda/cuda_attention_ops.cuh:6-22) and SentenceTransformer
+ * (include/sentence_transformers.h:12-40).  Each entry point below names the
+ * reference routine it replaces.  The C++ classes of the same names in this
+ * repository (include/ops/cuda/*, include/sentence_transformers.h) are thin
+ * wrappers over these functions.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  "device" pointers are CUDA device memory
+ *     owned by the caller; "host" pointers are ordinary host memory.
+ *   - Op entry points (fe_* without _engine) are stream-ordered, allocate nothing
+ *     and do not synchronise; the stream is a cudaStream_t (NULL = default).
+ *   - Every call returns an fe_status; fe_last_error_message() gives the detail
+ *     for the calling thread.  Nothing here calls exit() (the reference's matrix
+ *     ops do, src/ops/cuda/cuda_matrix_ops.cu:13-19).
+ *   - Device-side waits are bounded: a kernel whose wait runs out records
+ *     FE_ERR_DEVICE_TIMEOUT in a per-device status word and returns; read it with
+ *     fe_device_status().
+ */
+#ifndef FASTEMBED_B200_H
+#define FASTEMBED_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *fe_stream_t; /* identical to cudaStream_t */
+
+typedef enum fe_status {
+    FE_OK = 0,
+    FE_ERR_INVALID_ARGUMENT = 1, /* reference: std::invalid_argument */
+    FE_ERR_CUDA = 2,             /* reference: std::runtime_error from CUDA calls */
+    FE_ERR_OUT_OF_MEMORY = 3,
+    FE_ERR_UNSUPPORTED = 4,      /* shape or device this build does not handle */
+    FE_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait ran out */
+    FE_ERR_IO = 6,               /* file missing or malformed */
+    FE_ERR_NOT_FOUND = 7         /* unknown tensor name */
+} fe_status;
+
+/* Epilogues fused into the tensor-core linear layer. */
+typedef enum fe_epilogue {
+    FE_EPI_NONE = 0,          /* y = x W^T                          */
+    FE_EPI_BIAS = 1,          /* y = x W^T + b                      */
+    FE_EPI_BIAS_GELU = 2,     /* y = gelu_tanh(x W^T + b)           */
+    FE_EPI_BIAS_RELU = 3,     /* y = relu(x W^T + b)                */
+    FE_EPI_BIAS_SWISH = 4,    /* y = swish(x W^T + b)               */
+    FE_EPI_BIAS_RESIDUAL = 5  /* y = x W^T + b + residual (fp32)    */
+} fe_epilogue;
+
+typedef enum fe_dtype { FE_DTYPE_F32 = 0, FE_DTYPE_BF16 = 1 } fe_dtype;
+
+typedef enum fe_pooling {
+    FE_POOL_CLS = 0,  /* first token of each sentence (src/sentence_transformers_impl.cpp:289-290) */
+    FE_POOL_MEAN = 1, /* mean over valid tokens */
+    FE_POOL_LAST = 2  /* last valid token */
+} fe_pooling;
+
+typedef enum fe_activation { FE_ACT_GELU = 0, FE_ACT_RELU = 1, FE_ACT_SWISH = 2 } fe_activation;
+
+/* ---------------------------------------------------------------- status */
+const char *fe_status_string(fe_status s);
+/* Detail of the last failing call on this thread ("" if none). */
+const char *fe_last_error_message(void);
+/* Synchronises `device` and returns (then clears) its device-side status word:
+ * FE_OK, or FE_ERR_DEVICE_TIMEOUT when a kernel's bounded wait ran out. */
+fe_status fe_device_status(int device);
+/* Library version string. */
+const char *fe_version(void);
+
+/* ------------------------------------------- FP32 ops (legacy op API) ---
+ * Accurate FP32 SIMT kernels behind CUDAMatrixOps / CUDAAttentionOps, which
+ * the reference's GTests compare against the CPU ops at 1e-5 / 1e-3 absolute. */
+
+/* C[m,k] = A[m,n] · B[n,k].  Replaces CUDAMatrixOps::matrix_multiply
+ * (include/ops/cuda/cuda_matrix_ops.h:7-8, src/ops/cuda/cuda_matrix_ops.cu:192-219). */
+fe_status fe_sgemm_nn(const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                      fe_stream_t stream);
+/* C[m,k] = A[m,n] · B[k,n]^T (+ bias[k] when bias != NULL).  Replaces
+ * CUDAMatrixOps::matrix_multiply_transpose (cuda_matrix_ops.h:10-11, .cu:221-248). */
+fe_status fe_sgemm_nt(const float *a, const float *b, const float *bias, float *c, int64_t m,
+                      int64_t n, int64_t k, fe_stream_t stream);
+/* Elementwise activations.  Replace CUDAMatrixOps::gelu / relu / swish
+ * (cuda_matrix_ops.h:13-16, .cu:250-305); GELU is the tanh form. */
+fe_status fe_gelu_f32(const float *x, float *y, int64_t count, fe_stream_t stream);
+fe_status fe_relu_f32(const float *x, float *y, int64_t count, fe_stream_t stream);
+fe_status fe_swish_f32(const float *x, float *y, int64_t count, fe_stream_t stream);
+/* Row LayerNorm over `dim`, any dim >= 1.  Replaces CUDAMatrixOps::layer_norm
+ * (cuda_matrix_ops.h:18-22, .cu:307-362; the reference kernel needs dim <= 1024). */
+fe_status fe_layer_norm_f32(const float *x, const float *gamma, const float *beta, float *y,
+                            int64_t rows, int64_t dim, float eps, fe_stream_t stream);
+/* Row RMSNorm.  Replaces CUDAMatrixOps::rms_norm (cuda_matrix_ops.h:24-27, .cu:464-520). */
+fe_status fe_rms_norm_f32(const float *x, const float *weight, float *y, int64_t rows,
+                          int64_t dim, float eps, fe_stream_t stream);
+/* Row softmax, any dim.  Replaces CUDAMatrixOps::softmax(axis = 1)
+ * (cuda_matrix_ops.h:29, .cu:364-389). */
+fe_status fe_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t dim,
+                              fe_stream_t stream);
+/* In-place softmax over the last axis of [heads, seq_len, seq_len] device scores.
+ * Replaces CUDAMatrixOps::apply_softmax (cuda_matrix_ops.h:32, .cu:417-422). */
+fe_status fe_softmax_scores_inplace_f32(float *scores, int64_t heads, int64_t seq_len,
+                                        fe_stream_t stream);
+/* Bytes of device workspace fe_mha_f32 needs. */
+size_t fe_mha_f32_workspace_bytes(int64_t seq_len, int64_t dim, int64_t heads);
+/* Single-sequence MHA: Q,K,V = X·W^T + b, per head softmax(Q K^T / sqrt(hd)) V,
+ * heads concatenated.  Replaces CUDAAttentionOps::multi_head_attention
+ * (include/ops/cuda/cuda_attention_ops.cuh:10-20, src/ops/cuda/cuda_attention_ops.cu:164-342). */
+fe_status fe_mha_f32(const float *x, const float *wq, const float *wk, const float *wv,
+                     const float *bq, const float *bk, const float *bv, float *out,
+                     int64_t seq_len, int64_t dim, int64_t heads, void *workspace,
+                     size_t workspace_bytes, fe_stream_t stream);
+
+/* ----------------------------------- BF16 tensor-core hot-path ops -----
+ * tcgen05 (TMEM accumulator, TMA-fed) kernels of the model pipeline. */
+
+/* y[m,n] = epilogue(x[m,k] · w[n,k]^T): bf16 x and w (nn.Linear layout), FP32
+ * accumulation, fused bias / activation / residual; y is bf16 or fp32 (the
+ * residual form writes fp32).  Requires k % 8 == 0, n % 8 == 0, 16-byte aligned
+ * pointers.  Replaces the model's matrix_multiply_transpose calls plus their host
+ * bias / activation / residual loops (src/sentence_transformers_impl.cpp:250-263,
+ * :403-436). */
+fe_status fe_linear_bf16(const void *x, const void *w, const float *bias, const float *residual,
+                         void *y, int64_t m, int64_t n, int64_t k, fe_epilogue epilogue,
+                         fe_dtype y_dtype, fe_stream_t stream);
+/* Variable-length bidirectional attention over a packed batch.  qkv is bf16
+ * [total_tokens, 3*heads*head_dim] (Q | K | V column blocks, head h at h*head_dim);
+ * cu_seqlens (device, int32 [batch+1]) are sentence offsets; out is bf16
+ * [total_tokens, heads*head_dim].  Keys past a sentence's end are masked, which is
+ * the unpadded per-sentence attention of src/ops/cpu/cpu_attention_ops.cpp:33-85.
+ * head_dim must be 64; max_len <= 4096. */
+fe_status fe_attention_varlen_bf16(const void *qkv, const int32_t *cu_seqlens, int32_t batch,
+                                   int32_t max_len, int32_t heads, int32_t head_dim, void *out,
+                                   int64_t total_tokens, fe_stream_t stream);
+/* Fused embedding sum + LayerNorm over a packed batch: x_t = word[id_t] +
+ * pos[t - start(s)] + type[0]; writes LN(x) as fp32 (h32) and bf16 (h16).
+ * Replaces src/sentence_transformers_impl.cpp:30-44, :155-194.  Out-of-range ids
+ * and positions set FE_ERR_INVALID_ARGUMENT in the device status word and write
+ * zeros for that token. */
+fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int32_t batch,
+                             int64_t total_tokens, const float *word, const float *pos,
+                             const float *type, const float *gamma, const float *beta,
+                             int32_t dim, int32_t vocab, int32_t max_pos, float eps,
+                             float *h32, void *h16, fe_stream_t stream);
+/* Row LayerNorm writing fp32 and (when h16 != NULL) bf16 copies; the post-residual
+ * norms of src/sentence_transformers_impl.cpp:266 and :437. */
+fe_status fe_layernorm_dual(const float *x, const float *gamma, const float *beta, float *h32,
+                            void *h16, int64_t rows, int32_t dim, float eps, fe_stream_t stream);
+/* Per-sentence pooling + L2 normalisation of packed hidden states h [total, dim]
+ * into out [batch, dim].  Replaces src/sentence_transformers_impl.cpp:289-341. */
+fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, int32_t dim,
+                     fe_pooling mode, float *out, fe_stream_t stream);
+
+/* --------------------------------------------------------- model engine
+ * Device-resident post-LN BERT encoder (the reference's bge_forward,
+ * src/sentence_transformers_impl.cpp:126-344, batched and packed). */
+typedef struct fe_encoder_config {
+    int32_t vocab_size, hidden, layers, heads, intermediate, max_position, type_vocab;
+    float layer_norm_eps;
+    int32_t activation; /* fe_activation */
+    int32_t pooling;    /* fe_pooling */
+} fe_encoder_config;
+
+typedef struct fe_engine fe_engine;
+
+typedef struct fe_engine_stats {
+    int64_t launches;      /* kernels launched by the last encode call            */
+    int64_t gemm_launches; /* of which tcgen05 linear-layer kernels               */
+    int64_t tokens;        /* packed tokens of the last encode call               */
+    double gemm_ms;        /* summed device time of the linear-layer kernels      */
+    double attention_ms;   /* summed device time of the attention kernels         */
+    double other_ms;       /* summed device time of the memory-bound kernels      */
+    double gemm_flops;     /* algorithmic FLOPs of the linear layers (valid rows) */
+    double attention_flops;/* algorithmic FLOPs of QK^T and PV (valid keys)       */
+} fe_engine_stats;
+
+/* Creates an engine on `device` and allocates its weight storage.  Mirrors the
+ * SentenceTransformerImpl constructor (src/sentence_transformers_impl.cpp:46-98). */
+fe_status fe_engine_create(const fe_encoder_config *cfg, int device, fe_engine **out);
+fe_status fe_engine_destroy(fe_engine *e);
+/* Uploads one FP32 tensor by its HF name (the keys of the reference's weights map,
+ * src/sentence_transformers_impl.cpp:201-218).  `data` is host memory unless
+ * data_on_device != 0.  Unknown names return FE_ERR_NOT_FOUND; a wrong element
+ * count FE_ERR_INVALID_ARGUMENT. */
+fe_status fe_engine_set_weight(fe_engine *e, const char *name, const float *data, size_t count,
+                               int data_on_device);
+/* Loads every tensor of a model.safetensors file (F32 or BF16 entries); returns
+ * FE_ERR_IO on a malformed file.  Replaces load_single_safetensors_file
+ * (src/safetensors.cpp:31-95). */
+fe_status fe_engine_load_safetensors(fe_engine *e, const char *path);
+/* Number of weights still unset (0 = ready). */
+int32_t fe_engine_missing_weights(const fe_engine *e);
+/* Encodes a packed batch already resident on the engine's device: ids (int32
+ * [total]) and cu_seqlens (int32 [batch+1]) are device pointers; cu_seqlens_host
+ * is the same offsets in host memory (they size the launches); out is device
+ * fp32 [batch, hidden].  Stream-ordered on `stream` (NULL = the engine's stream);
+ * does not synchronise. */
+fe_status fe_engine_encode_packed(fe_engine *e, const int32_t *ids, const int32_t *cu_seqlens,
+                                  const int32_t *cu_seqlens_host, int32_t batch, float *out,
+                                  fe_stream_t stream);
+/* End-to-end encode from host buffers: ids is host int32 [batch, stride] (right
+ * padded), lengths host int32 [batch]; out is host fp32 [batch, hidden].  Copies
+ * in, runs, copies out and synchronises.  The token-id form of
+ * SentenceTransformerImpl::encode_batch (src/sentence_transformers_impl.cpp:359-365). */
+fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t *lengths,
+                                int32_t batch, int32_t stride, float *out);
+/* Per-kernel device timing of subsequent encode calls (CUDA events on the
+ * launching stream); off by default. */
+fe_status fe_engine_set_profiling(fe_engine *e, int enabled);
+fe_status fe_engine_get_stats(const fe_engine *e, fe_engine_stats *stats);
+
+/* ------------------------------------------------------ host-only helpers */
+/* Contiguous cut points of a length-sorted batch into `parts` slices of near-equal
+ * algorithmic FLOPs (parts-1 cuts written to `cuts`).  Host only; no GPU needed. */
+fe_status fe_plan_shards(const fe_encoder_config *cfg, const int32_t *sorted_lengths,
+                         int32_t batch, int32_t parts, int32_t *cuts);
+/* Packs right-padded host ids [batch, stride] with lengths into ids_packed
+ * [sum(lengths)] and cu_seqlens [batch+1].  Host only. */
+fe_status fe_pack_batch(const int32_t *ids, const int32_t *lengths, int32_t batch,
+                        int32_t stride, int32_t *ids_packed, int32_t *cu_seqlens);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FASTEMBED_B200_H */

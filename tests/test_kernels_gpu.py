@@ -1,0 +1,231 @@
+"""Parity of each CUDA kernel, called through the C ABI, on a B200.
+
+Floating-point kernels are compared with a plain PyTorch fp32 computation on the
+same (bf16-rounded, where the kernel takes bf16) inputs; the tolerance is written
+beside each check.  Index work (sentence offsets, positions, pooled rows) must be
+exact and is checked with equality."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel_err(a, b):
+    return float((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-12))
+
+
+# ------------------------------------------------------------ tcgen05 linear
+LINEAR_SHAPES = [
+    (1, 128, 64),       # single row, BN=128 tile, one k-block
+    (130, 256, 64),     # ragged M tail
+    (200, 384, 128),    # N = 3 x 128 -> BN=128
+    (333, 1024, 1024),  # out-proj shape, ragged M
+    (1000, 3072, 1024), # QKV shape
+    (257, 4096, 1024),  # FFN1 shape
+    (129, 1024, 4096),  # FFN2 shape (long K)
+    (64, 512, 72),      # K not a multiple of 64 (TMA zero fill)
+    (96, 1000, 64),     # N not a multiple of 64 (clipped store)
+]
+
+
+@pytest.mark.parametrize("m,n,k", LINEAR_SHAPES)
+@pytest.mark.parametrize("epi,out", [("none", "f32"), ("bias", "bf16"), ("bias_gelu", "bf16"),
+                                     ("bias_residual", "f32")])
+def test_linear_bf16(cuda_dev, m, n, k, epi, out):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, device=cuda_dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    bias = torch.randn(n, device=cuda_dev, generator=g) * 0.1
+    res = torch.randn(m, n, device=cuda_dev, generator=g)
+    y = ops.linear_bf16(x, w, bias if epi != "none" else None, res if epi == "bias_residual" else None, epi, out)
+    ref = x.float() @ w.float().T
+    if epi != "none":
+        ref = ref + bias
+    if epi == "bias_gelu":
+        ref = 0.5 * ref * (1 + torch.tanh(math.sqrt(2 / math.pi) * (ref + 0.044715 * ref ** 3)))
+    if epi == "bias_residual":
+        ref = ref + res
+    torch.cuda.synchronize()
+    # fp32 out: only the accumulation order differs -> 1e-4 relative to the output scale;
+    # bf16 out: one bf16 rounding (2^-8 relative) plus the hardware tanh -> 1e-2.
+    tol = 1e-4 if out == "f32" else 1e-2
+    assert _rel_err(y, ref) < tol
+    ops.device_status(0)
+
+
+def test_linear_rejects_bad_shapes(cuda_dev):
+    from fastembed_b200 import ops
+    from fastembed_b200.capi import FeError
+    x = torch.zeros(4, 60, dtype=torch.bfloat16, device=cuda_dev)
+    w = torch.zeros(8, 60, dtype=torch.bfloat16, device=cuda_dev)
+    with pytest.raises(FeError):  # k % 8 != 0
+        ops.linear_bf16(x, w)
+    with pytest.raises(FeError):  # the residual epilogue needs a residual
+        ops.linear_bf16(torch.zeros(4, 64, dtype=torch.bfloat16, device=cuda_dev),
+                        torch.zeros(8, 64, dtype=torch.bfloat16, device=cuda_dev),
+                        torch.zeros(8, device=cuda_dev), None, "bias_residual", "f32")
+
+
+def test_linear_deterministic_and_row_independent(cuda_dev):
+    """Each output row depends only on its own input row: computing a row block
+    alone gives bit-identical results (the batch-invariance the engine relies on)."""
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(3)
+    x = torch.randn(700, 1024, device=cuda_dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(3072, 1024, device=cuda_dev, generator=g) / 32).to(torch.bfloat16)
+    b = torch.randn(3072, device=cuda_dev, generator=g)
+    y1 = ops.linear_bf16(x, w, b, None, "bias", "bf16")
+    y2 = ops.linear_bf16(x, w, b, None, "bias", "bf16")
+    y3 = ops.linear_bf16(x[300:437].contiguous(), w, b, None, "bias", "bf16")
+    assert torch.equal(y1, y2)
+    assert torch.equal(y1[300:437], y3)
+
+
+# ------------------------------------------------------------ varlen attention
+def _attn_ref(qkv, lens, heads, hd=64):
+    D = heads * hd
+    out = torch.zeros(qkv.shape[0], D, device=qkv.device)
+    s = 0
+    for L in lens:
+        q = qkv[s:s + L, :D].float().view(L, heads, hd).transpose(0, 1)
+        k = qkv[s:s + L, D:2 * D].float().view(L, heads, hd).transpose(0, 1)
+        v = qkv[s:s + L, 2 * D:].float().view(L, heads, hd).transpose(0, 1)
+        p = torch.softmax(q @ k.transpose(1, 2) / math.sqrt(hd), dim=-1)
+        out[s:s + L] = (p @ v).transpose(0, 1).reshape(L, D)
+        s += L
+    return out
+
+
+@pytest.mark.parametrize("lens,heads", [
+    ([1], 1), ([7, 1, 63], 2), ([64, 65, 127, 128, 129], 4), ([200, 255, 256, 257], 16),
+    ([512, 3, 511, 300], 12), ([96] * 40, 16)])
+def test_attention_varlen(cuda_dev, lens, heads):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(sum(lens) + heads)
+    T = sum(lens)
+    qkv = torch.randn(T, 3 * heads * 64, device=cuda_dev, generator=g).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    out = ops.attention_varlen(qkv, cu, max(lens), heads)
+    ref = _attn_ref(qkv, lens, heads)
+    torch.cuda.synchronize()
+    # P is rounded to bf16 before PV (2^-9 relative per weight) and O to bf16: 2e-2 abs on unit-scale V.
+    assert float((out.float() - ref).abs().max()) < 2e-2
+    ops.device_status(0)
+
+
+def test_attention_sharp_softmax(cuda_dev):
+    """Large scores (near one-hot rows) exercise the online max / rescale across key tiles."""
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(11)
+    lens = [300, 129, 17]
+    T = sum(lens)
+    qkv = (torch.randn(T, 3 * 2 * 64, device=cuda_dev, generator=g) * 3).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    out = ops.attention_varlen(qkv, cu, max(lens), 2)
+    ref = _attn_ref(qkv, lens, 2)
+    assert float((out.float() - ref).abs().max()) < 6e-2  # |V| up to ~12: 2^-8 relative of the output scale
+
+
+# ------------------------------------------------------------ row kernels
+def test_embed_layernorm_exact_indexing(cuda_dev):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(5)
+    V, P, D = 1000, 512, 1024
+    word = torch.randn(V, D, device=cuda_dev, generator=g)
+    pos = torch.randn(P, D, device=cuda_dev, generator=g)
+    typ = torch.randn(2, D, device=cuda_dev, generator=g)
+    gam = torch.rand(D, device=cuda_dev, generator=g) + 0.5
+    bet = torch.randn(D, device=cuda_dev, generator=g)
+    lens = [1, 5, 512, 33]
+    ids = torch.randint(0, V, (sum(lens),), device=cuda_dev, generator=g, dtype=torch.int32)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    h32, h16 = ops.embed_layernorm(ids, cu, word, pos, typ, gam, bet, 1e-12)
+    posids = torch.cat([torch.arange(L, device=cuda_dev) for L in lens])
+    x = word[ids.long()] + pos[posids] + typ[0]
+    mu = x.mean(-1, keepdim=True)
+    var = ((x - mu) ** 2).mean(-1, keepdim=True)
+    ref = (x - mu) / torch.sqrt(var + 1e-12) * gam + bet
+    assert float((h32 - ref).abs().max()) < 5e-5
+    assert torch.equal(h16, h32.to(torch.bfloat16))
+
+
+def test_layernorm_dual(cuda_dev):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(6)
+    for D in (512, 768, 1024, 640):
+        x = torch.randn(777, D, device=cuda_dev, generator=g) * 3 + 1
+        gam = torch.randn(D, device=cuda_dev, generator=g)
+        bet = torch.randn(D, device=cuda_dev, generator=g)
+        h32, h16 = ops.layernorm_dual(x, gam, bet, 1e-12)
+        ref = torch.nn.functional.layer_norm(x, (D,), gam, bet, 1e-12)
+        assert float((h32 - ref).abs().max()) < 1e-4
+        assert torch.equal(h16, h32.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("mode", ["cls", "mean", "last"])
+def test_pool_l2_indices(cuda_dev, mode):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(9)
+    lens = [1, 9, 128, 2]
+    D = 768
+    h = torch.randn(sum(lens), D, device=cuda_dev, generator=g)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    out = ops.pool_l2(h, cu, mode)
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    for b, (s, L) in enumerate(zip(starts, lens)):
+        if mode == "cls":
+            v = h[s]
+        elif mode == "last":
+            v = h[s + L - 1]
+        else:
+            v = h[s:s + L].mean(0)
+        v = v / v.norm()
+        tol = 0 if mode != "mean" else 1e-5
+        assert float((out[b] - v).abs().max()) <= tol + 1e-7
+
+
+# ------------------------------------------------------------ fp32 op API
+def test_fp32_ops_match_oracle(cuda_dev, oracle_lib):
+    from fastembed_b200 import ops
+    O = oracle_lib
+    rng = np.random.default_rng(0)
+    for (m, n, k) in [(2, 2, 2), (4, 5, 6), (16, 16, 16), (1, 1, 1), (100, 200, 300), (65, 130, 70)]:
+        a = rng.uniform(-1, 1, m * n).astype(np.float32)
+        b = rng.uniform(-1, 1, n * k).astype(np.float32)
+        ta, tb = torch.tensor(a, device=cuda_dev), torch.tensor(b, device=cuda_dev)
+        # the CPU ops' dot-product order is reproduced exactly
+        assert np.array_equal(ops.sgemm_nn(ta, tb, m, n, k).cpu().numpy(), O.matmul_nn(a, b, m, n, k))
+        assert np.array_equal(ops.sgemm_nt(ta, tb, m, n, k).cpu().numpy(), O.matmul_nt(a, b, m, n, k))
+    x = rng.uniform(-4, 4, 100000).astype(np.float32)
+    tx = torch.tensor(x, device=cuda_dev)
+    for name in ("gelu", "relu", "swish"):
+        assert np.abs(ops.unary(name, tx).cpu().numpy() - O.unary(name, x)).max() < 1e-6
+    for D in (16, 1024, 3000):
+        xs = rng.uniform(-1, 1, 10 * D).astype(np.float32)
+        gm = rng.uniform(-1, 1, D).astype(np.float32)
+        bt = rng.uniform(-1, 1, D).astype(np.float32)
+        t = lambda v: torch.tensor(v, device=cuda_dev)
+        for eps in (1e-5, 1e-10):
+            assert np.abs(ops.layer_norm_f32(t(xs), t(gm), t(bt), D, eps).cpu().numpy()
+                          - O.layer_norm(xs, gm, bt, D, eps)).max() < 1e-5
+        assert np.abs(ops.rms_norm_f32(t(xs), t(gm), D, 1e-6).cpu().numpy() - O.rms_norm(xs, gm, D, 1e-6)).max() < 1e-5
+        assert np.abs(ops.softmax_rows_f32(t(xs), D).cpu().numpy() - O.softmax_rows(xs, D)).max() < 1e-6
+
+
+def test_fp32_mha_matches_oracle_reference_inputs(cuda_dev, oracle_lib):
+    """tests/attention_ops_test.cpp's cases: every tensor is a fresh mt19937(42)
+    U(-1,1) stream, 1e-3 absolute."""
+    from fastembed_b200 import ops
+    O = oracle_lib
+    for (L, D, H) in [(10, 64, 4), (10, 128, 8), (10, 512, 16), (10, 1024, 16), (77, 256, 4)]:
+        x = O.uniform_mt19937(L * D)
+        w = O.uniform_mt19937(D * D)
+        b = O.uniform_mt19937(D)
+        ref = O.mha(x, w, w, w, b, b, b, H, D)
+        t = lambda v: torch.tensor(v, device=cuda_dev)
+        got = ops.mha_f32(t(x), t(w), t(w), t(w), t(b), t(b), t(b), H, D).cpu().numpy()
+        assert np.abs(got - ref).max() < 1e-3
