@@ -157,12 +157,14 @@ fe_status fe_attention_varlen_bf16(const void *qkv, const int32_t *cu_seqlens, i
     if (max_len > 4096 || heads > 65535 || batch > 65535)
         return fail(FE_ERR_UNSUPPORTED, "fe_attention_varlen_bf16: batch, heads or max_len too large");
     if (batch == 0 || total_tokens == 0) return FE_OK;
+    if (static_cast<int64_t>(4096) * ((max_len + 127) / 128) * heads > 0x7fffffff)
+        return fail(FE_ERR_UNSUPPORTED, "fe_attention_varlen_bf16: too many (sentence, tile, head) units");
     if (!qkv || !cu_seqlens || !out) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_bf16: null pointer");
     if (!aligned16(qkv) || !aligned16(out))
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_bf16: pointers must be 16-byte aligned");
     fe_status st = FE_OK;
     cudaError_t e = fe::launch_attention_varlen(qkv, cu_seqlens, batch, max_len, heads, head_dim, out, total_tokens,
-                                                reinterpret_cast<cudaStream_t>(stream), &st);
+                                                false, reinterpret_cast<cudaStream_t>(stream), &st);
     if (st != FE_OK) return st;
     return done(e, "fe_attention_varlen_bf16");
 }

@@ -277,7 +277,7 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
             Scope sc(e, CAT_ATTN, s);
             fe_status st = FE_OK;
             cudaError_t err = fe::launch_attention_varlen(qkv, cu, batch, max_len, c.heads,
-                                                          static_cast<int>(D / c.heads), attn, T, s, &st);
+                                                          static_cast<int>(D / c.heads), attn, T, false, s, &st);
             if (st != FE_OK) return st;
             FE_TRY_CUDA(err);
         }

@@ -46,13 +46,21 @@ fe_status make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType d
                        int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld,
                        uint32_t box_rows, uint32_t box_cols, bool swizzle128 = true);
 
+// TMA descriptor for a head-major tensor [heads, rows, 64] of bf16 (each head's
+// rows contiguous), box [1, box_rows, 64], 128B swizzle.
+fe_status make_tmap_heads(CUtensorMap *map, const void *base, uint64_t heads, uint64_t rows,
+                          uint32_t box_rows);
+
 // ---- launchers (no argument validation; the C ABI validates) ----
 cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
                                const float *residual, void *y, int64_t m, int64_t n, int64_t k,
                                int epilogue, int y_dtype, cudaStream_t s, fe_status *st);
+// qkv / out layouts: token-major [T, 3*H*64] / [T, H*64], or head-major
+// [3*H, T, 64] / [H, T, 64] when head_major is true.
 cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, int batch,
                                     int max_len, int heads, int head_dim, void *out,
-                                    int64_t total_tokens, cudaStream_t s, fe_status *st);
+                                    int64_t total_tokens, bool head_major, cudaStream_t s,
+                                    fe_status *st);
 cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
                                    const float *word, const float *pos, const float *type,
                                    const float *g, const float *b, int dim, int vocab,

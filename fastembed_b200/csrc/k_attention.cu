@@ -4,18 +4,27 @@
 // (src/ops/cuda/cuda_attention_ops.cu:264-313: permute, batched QK^T, scaled softmax,
 // batched PV, unpermute) for a packed batch of unpadded sentences.  Its semantics are
 // the CPU reference's per-sentence attention (src/ops/cpu/cpu_attention_ops.cpp:33-85):
-// softmax(Q K^T / sqrt(hd)) V with keys limited to the sentence, which is exactly a
-// key-padding mask over a padded batch.
+// softmax(Q K^T / sqrt(hd)) V with keys limited to the sentence, i.e. a key-padding
+// mask over a padded batch.
 //
-// One CTA = (128-query tile, sentence, head); 4 warps, thread t owns query row t.
-//   * TMA reads Q, K, V tiles [128 x 64] straight out of the packed QKV GEMM output
-//     (column block h*64 of the Q / K / V thirds), so there is no permute pass.
-//   * S = Q K^T (M=128, N=128, K=64) lands in TMEM; each thread reads its row with
-//     tcgen05.ld, masks keys past the sentence end, runs the online-softmax update in
-//     registers and writes P (bf16) into a 128B-swizzled shared-memory tile.
-//   * O_j = P V_j (M=128, N=64, K=128, V as an MN-major operand) lands in TMEM; the
-//     thread folds it into its fp32 accumulator with the running rescale factor.
-// Waits are bounded (device status word on timeout).
+// Persistent, warp-specialised (one CTA per SM).  A work unit is (sentence, 128-row
+// query tile, head); an item is one 128-key tile of a unit.  All roles walk the same
+// unit sequence (blockIdx.x, +gridDim.x, ...) and skip query tiles past a sentence's end.
+//   warp 0     TMA producer: Q tile per unit into a 2-slot ring, K/V tiles per item into
+//              a 4-slot ring, read straight from the packed QKV buffer (no permute);
+//              tiles of the next units are prefetched into L2 ahead of the loads, so
+//              DRAM latency stays off the per-item chain.
+//   warp 1     TMEM owner + MMA issuer: S = Q K^T (M=128, N = keys rounded up to 16)
+//              into one of two TMEM S buffers; then, for the previous item, O = P V
+//              with P read from TMEM (A operand) and V as an MN-major smem operand.
+//   warps 2-9  two softmax warpgroups taking alternate units (ping-pong), each with
+//              its own TMEM S/P and O buffers: thread = query row; reads its S row
+//              (tcgen05.ld), masks keys past the sentence end, online max / sum, writes
+//              P (bf16) back over S (tcgen05.st); one item later folds O into fp32
+//              registers and, after a unit's last item, stores O / l.
+// One warpgroup's softmax overlaps the other's and the tensor core's S / PV.  Waits are
+// bounded; on timeout the CTA records FE_ERR_DEVICE_TIMEOUT, drains what it started
+// and exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -26,12 +35,17 @@ namespace fe {
 namespace {
 
 constexpr int HD = 64;
-constexpr int TQ = 128;  // query rows per CTA
-constexpr int TK = 128;  // keys per inner tile
-constexpr uint32_t TILE_BYTES = 128 * HD * 2;  // 16 KB: [128 rows x 64] bf16
-constexpr uint32_t P_BYTES = TQ * TK * 2;      // 32 KB
-constexpr uint32_t SMEM_BYTES = 1024 + 3 * TILE_BYTES + P_BYTES + 128;
-constexpr uint32_t TMEM_COLS = 256;  // S at [0,128), O at [128,192)
+constexpr int TQ = 128;
+constexpr int TK = 128;
+constexpr int Q_SLOTS = 2;
+constexpr int KV_SLOTS = 4;
+constexpr int kPrefetchItems = 8;  // key tiles the producer keeps requested into L2 ahead of its loads
+constexpr uint32_t Q_BYTES = TQ * HD * 2;       // 16 KB
+constexpr uint32_t KV_BYTES = 2 * TK * HD * 2;  // K then V, 32 KB
+constexpr int kMaxUnits = 2048;  // per-CTA list of valid units, built at kernel start
+constexpr uint32_t SMEM_BYTES = 1024 + Q_SLOTS * Q_BYTES + KV_SLOTS * KV_BYTES + 512 + 12 * kMaxUnits + 64;
+constexpr uint32_t TMEM_COLS = 512;  // S/P of warpgroup g at g*128, its O at 256 + g*64
+constexpr int kThreads = 64 + 256;
 
 __device__ __forceinline__ float fast_exp2(float x)
 {
@@ -40,40 +54,76 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
-__global__ void __launch_bounds__(128)
-    attn_varlen_tcgen05(const __grid_constant__ CUtensorMap tm_qkv, const int32_t *__restrict__ cu_seqlens,
-                        int dim, __nv_bfloat16 *__restrict__ out, float scale_log2, int *status)
-{
-    const int seq = blockIdx.y;
-    const int head = blockIdx.z;
-    const int start = cu_seqlens[seq];
-    const int len = cu_seqlens[seq + 1] - start;
-    const int q0 = blockIdx.x * TQ;
-    if (q0 >= len) return;  // whole CTA leaves before touching TMEM or barriers
+struct Unit {
+    int start, len, q0, head, n_kv;
+};
 
+// A CTA's k-th valid unit, from the list built at kernel start: entry = {first row of
+// the sentence, sentence length, (head << 8) | query tile}.
+__device__ __forceinline__ Unit unit_at(const int3 *list, int k)
+{
+    const int3 e = list[k];
+    Unit w;
+    w.start = e.x;
+    w.len = e.y;
+    w.head = e.z >> 8;
+    w.q0 = (e.z & 255) * TQ;
+    w.n_kv = (w.len + TK - 1) / TK;
+    return w;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_varlen_tcgen05(const __grid_constant__ CUtensorMap tm_qkv, const int32_t *__restrict__ cu_seqlens,
+                        int batch, int heads, int qtiles, __nv_bfloat16 *__restrict__ out, float scale_log2,
+                        int total_tokens, int head_major, int *status)
+{
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sQ = smem;
-    uint8_t *sK = sQ + TILE_BYTES;
-    uint8_t *sV = sK + TILE_BYTES;
-    uint8_t *sP = sV + TILE_BYTES;
-    uint64_t *bar_ld = reinterpret_cast<uint64_t *>(sP + P_BYTES);
-    uint64_t *bar_s = bar_ld + 1;
-    uint64_t *bar_o = bar_ld + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_ld + 3);
+    uint8_t *sKV = sQ + Q_SLOTS * Q_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sKV + KV_SLOTS * KV_BYTES);
+    uint64_t *q_full = bars;                  // [2]
+    uint64_t *q_empty = q_full + Q_SLOTS;     // [2]
+    uint64_t *kv_full = q_empty + Q_SLOTS;    // [3]
+    uint64_t *kv_empty = kv_full + KV_SLOTS;  // [3]
+    uint64_t *s_full = kv_empty + KV_SLOTS;   // [2]
+    uint64_t *p_full = s_full + 2;            // [2]
+    uint64_t *s_free = p_full + 2;            // [2]
+    uint64_t *o_full = s_free + 2;            // [2]
+    uint64_t *o_empty = o_full + 2;           // [2]
+    uint64_t *probe = o_empty + 2;            // [1]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(probe + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int3 *ulist = reinterpret_cast<int3 *>(reinterpret_cast<uint8_t *>(bars) + 512);
+    int *warp_tot = reinterpret_cast<int *>(ulist + kMaxUnits);  // [10] + count
 
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    const int n_kv = (len + TK - 1) / TK;
-    const int qcol = head * HD, kcol = dim + head * HD, vcol = 2 * dim + head * HD;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int dim = heads * HD;
+    const int units = batch * qtiles * heads;
 
-    if (tid == 0) {
-        mbar_init(bar_ld, 1);
-        mbar_init(bar_s, 1);
-        mbar_init(bar_o, 1);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < Q_SLOTS; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+        }
+        for (int i = 0; i < KV_SLOTS; ++i) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 4);  // one arrival per softmax warp
+            mbar_init(&s_free[i], 1);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&o_empty[i], 4);
+        }
+        mbar_init(probe, 1);
+        *abort_flag = 0;
         fence_mbar_init();
+        tma_prefetch_desc(&tm_qkv);
     }
-    if (warp == 0) {
+    if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
@@ -81,156 +131,327 @@ __global__ void __launch_bounds__(128)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem + t_lane;
-    const uint32_t tO = tmem + t_lane + 128;
 
-    // Only thread 0 issues TMA loads and MMAs; `arms` counts the loads it armed on
-    // bar_ld and `landed` those it has seen complete.
-    int arms = 0, landed = 0;
-    uint64_t *open_bar = nullptr;  // barrier of a committed MMA not yet seen complete
-    uint32_t open_par = 0;
-    if (tid == 0) {
-        mbar_arrive_expect_tx(bar_ld, 3 * TILE_BYTES);
-        tma_load_2d(sQ, &tm_qkv, bar_ld, qcol, start + q0);
-        tma_load_2d(sK, &tm_qkv, bar_ld, kcol, start);
-        tma_load_2d(sV, &tm_qkv, bar_ld, vcol, start);
-        arms = 1;
+    // Unit u = blockIdx.x + i * gridDim.x is (sentence u / (H*QT), query tile (u / H) % QT,
+    // head u % H); keep, in order, those whose query tile starts inside the sentence.
+    {
+        const int ncand = units > static_cast<int>(blockIdx.x) ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+        const int nwarps = blockDim.x >> 5;
+        int base = 0;
+        for (int c0 = 0; c0 < ncand; c0 += blockDim.x) {
+            const int ci = c0 + threadIdx.x;
+            bool valid = false;
+            int3 e = make_int3(0, 0, 0);
+            if (ci < ncand) {
+                const int u = blockIdx.x + ci * gridDim.x;
+                const int hh = u % heads;
+                const int t = (u / heads) % qtiles;
+                const int sidx = u / (heads * qtiles);
+                const int st = cu_seqlens[sidx];
+                const int ln = cu_seqlens[sidx + 1] - st;
+                valid = t * TQ < ln;
+                e = make_int3(st, ln, (hh << 8) | t);
+            }
+            const unsigned bal = __ballot_sync(0xffffffffu, valid);
+            if (lane == 0) warp_tot[warp] = __popc(bal);
+            __syncthreads();
+            int off = base, total = 0;
+            for (int w2 = 0; w2 < nwarps; ++w2) {
+                if (w2 < warp) off += warp_tot[w2];
+                total += warp_tot[w2];
+            }
+            const int pos = off + __popc(bal & ((1u << lane) - 1));
+            if (valid && pos < kMaxUnits) ulist[pos] = e;
+            base += total;
+            __syncthreads();
+        }
+        if (base > kMaxUnits) {
+            if (threadIdx.x == 0) report(status, DEV_BAD_INPUT);
+            base = 0;  // refuse the work rather than drop part of it
+        }
+        if (threadIdx.x == 0) warp_tot[nwarps] = base;
+        __syncthreads();
     }
+    const int nlist = warp_tot[blockDim.x >> 5];
 
-    constexpr uint32_t idesc_s = idesc_bf16_f32(TQ, TK, false, false);
-    constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
-    float m_run = -INFINITY, l_run = 0.f;
-    float o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = 0.f;
-    bool aborted = false;
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (mbar_wait(bar, parity)) return true;
+        report(status, DEV_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+    };
+    // Tile `which` (0 = Q, 1 = K, 2 = V) of `head`, rows [row, row + 128): one 128-byte
+    // row per token in the token-major layout, or a contiguous 16 KB block head-major.
+    auto load_tile = [&](void *dst, uint64_t *bar, int which, int head, int row) {
+        if (head_major) tma_load_3d(dst, &tm_qkv, bar, 0, row, which * heads + head);
+        else tma_load_2d(dst, &tm_qkv, bar, which * dim + head * HD, row);
+    };
+    auto prefetch_tile = [&](int which, int head, int row) {
+        if (head_major) tma_prefetch_l2_3d(&tm_qkv, 0, row, which * heads + head);
+        else tma_prefetch_l2_2d(&tm_qkv, which * dim + head * HD, row);
+    };
 
-    for (int j = 0; j < n_kv; ++j) {
-        const uint32_t par = j & 1;
-        bool to = false;
-        if (tid == 0) {
-            to = !mbar_wait(bar_ld, par);
-            if (!to) {
-                landed = arms;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            uint32_t qn = 0, kvn = 0;
+            uint32_t q_armed = 0, kv_armed = 0, q_par = 0, kv_par = 0;
+            bool ok = true;
+            int pf_k = 0;           // next list entry to prefetch into L2
+            uint32_t pf_items = 0;  // key tiles prefetched so far
+            for (int k = 0; k < nlist && ok && !*abort_flag; ++k) {
+                const Unit w = unit_at(ulist, k);
+                while (pf_items < kvn + kPrefetchItems && pf_k < nlist) {
+                    const Unit pw = unit_at(ulist, pf_k++);
+                    prefetch_tile(0, pw.head, pw.start + pw.q0);
+                    for (int j = 0; j < pw.n_kv; ++j) {
+                        prefetch_tile(1, pw.head, pw.start + j * TK);
+                        prefetch_tile(2, pw.head, pw.start + j * TK);
+                    }
+                    pf_items += pw.n_kv;
+                }
+                const int qs = qn % Q_SLOTS;
+                if (!(ok = wait(&q_empty[qs], ((qn / Q_SLOTS) & 1) ^ 1))) break;
+                mbar_arrive_expect_tx(&q_full[qs], Q_BYTES);
+                load_tile(sQ + qs * Q_BYTES, &q_full[qs], 0, w.head, w.start + w.q0);
+                q_armed |= 1u << qs;
+                q_par = (q_par & ~(1u << qs)) | (((qn / Q_SLOTS) & 1) << qs);
+                ++qn;
+                for (int j = 0; j < w.n_kv; ++j) {
+                    const int ks = kvn % KV_SLOTS;
+                    if (!(ok = wait(&kv_empty[ks], ((kvn / KV_SLOTS) & 1) ^ 1))) break;
+                    uint8_t *dst = sKV + ks * KV_BYTES;
+                    mbar_arrive_expect_tx(&kv_full[ks], KV_BYTES);
+                    load_tile(dst, &kv_full[ks], 1, w.head, w.start + j * TK);
+                    load_tile(dst + KV_BYTES / 2, &kv_full[ks], 2, w.head, w.start + j * TK);
+                    kv_armed |= 1u << ks;
+                    kv_par = (kv_par & ~(1u << ks)) | (((kvn / KV_SLOTS) & 1) << ks);
+                    ++kvn;
+                }
+            }
+            // every load this thread started lands before the CTA exits
+            for (int i = 0; i < Q_SLOTS; ++i)
+                if ((q_armed >> i) & 1) (void)mbar_wait(&q_full[i], (q_par >> i) & 1);
+            for (int i = 0; i < KV_SLOTS; ++i)
+                if ((kv_armed >> i) & 1) (void)mbar_wait(&kv_full[i], (kv_par >> i) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
+            uint32_t qn = 0, kvn = 0, nunit = 0;
+            uint32_t itg[2] = {0, 0};  // items issued per softmax warpgroup
+            bool issued = false, ok = true, have_pend = false;
+            uint32_t pend_g = 0, pend_it = 0, pend_ks = 0;
+            int pend_valid = 0;
+            // O[g] = P[g] V for warpgroup g's item `pit` (P from TMEM, V MN-major from smem)
+            auto issue_pv = [&](uint32_t g, uint32_t pit, uint32_t pks, int pvalid) -> bool {
+                if (!wait(&p_full[g], pit & 1)) return false;
+                if (!wait(&o_empty[g], (pit & 1) ^ 1)) return false;
                 tc_fence_after();
-                const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK);
+                const uint32_t v_addr = smem_u32(sKV + pks * KV_BYTES + KV_BYTES / 2);
+                const int nks = (pvalid + 15) >> 4;
+                for (int ks = 0; ks < nks; ++ks)
+                    umma_f16_ts(tmem + 256 + g * 64, tmem + g * 128 + ks * 8,
+                                sdesc_sw128(v_addr + ks * 16 * 128, TK * 128, 1024), idesc_o, ks != 0 ? 1u : 0u);
+                umma_commit(&o_full[g]);
+                umma_commit(&s_free[g]);
+                umma_commit(&kv_empty[pks]);
+                return true;
+            };
+            for (int k = 0; k < nlist && ok && !*abort_flag; ++k) {
+                const Unit w = unit_at(ulist, k);
+                const uint32_t g = nunit++ & 1;
+                const int qs = qn % Q_SLOTS;
+                if (!(ok = wait(&q_full[qs], (qn / Q_SLOTS) & 1))) break;
+                const uint32_t q_addr = smem_u32(sQ + qs * Q_BYTES);
+                for (int j = 0; j < w.n_kv; ++j) {
+                    const uint32_t ks = kvn % KV_SLOTS;
+                    const uint32_t it = itg[g];
+                    if (!(ok = wait(&kv_full[ks], (kvn / KV_SLOTS) & 1))) break;
+                    // this warpgroup's previous item must finish PV before S reuses its TMEM
+                    if (have_pend && pend_g == g) {
+                        if (!(ok = issue_pv(pend_g, pend_it, pend_ks, pend_valid))) break;
+                        have_pend = false;
+                    }
+                    if (!(ok = wait(&s_free[g], (it & 1) ^ 1))) break;
+                    tc_fence_after();
+                    const int valid = min(TK, w.len - j * TK);
+                    const int n = min(TK, max(16, (valid + 15) & ~15));
+                    const uint32_t idesc_s = idesc_bf16_f32(TQ, n, false, false);
+                    const uint32_t k_addr = smem_u32(sKV + ks * KV_BYTES);
 #pragma unroll
-                for (int k = 0; k < HD / 16; ++k)
-                    umma_f16_ss(tmem, sdesc_sw128(q_addr + k * 32, 16, 1024),
-                                sdesc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
-                umma_commit(bar_s);
-                open_bar = bar_s;
-                open_par = par;
+                    for (int k = 0; k < HD / 16; ++k)
+                        umma_f16_ss(tmem + g * 128, sdesc_sw128(q_addr + k * 32, 16, 1024),
+                                    sdesc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
+                    issued = true;
+                    umma_commit(&s_full[g]);
+                    if (j == w.n_kv - 1) umma_commit(&q_empty[qs]);
+                    if (have_pend && !(ok = issue_pv(pend_g, pend_it, pend_ks, pend_valid))) break;
+                    have_pend = true;
+                    pend_g = g;
+                    pend_it = it;
+                    pend_ks = ks;
+                    pend_valid = valid;
+                    itg[g] = it + 1;
+                    ++kvn;
+                }
+                ++qn;
+            }
+            if (ok && have_pend && !*abort_flag) ok = issue_pv(pend_g, pend_it, pend_ks, pend_valid);
+            if (issued) {
+                // all MMAs issued by this thread retire before TMEM is released
+                umma_commit(probe);
+                (void)mbar_wait(probe, 0);
             }
         }
-        if (__syncthreads_or(to)) { aborted = true; break; }
-        to = !mbar_wait(bar_s, par);
-        if (__syncthreads_or(to)) { aborted = true; break; }
-        open_bar = nullptr;
-        tc_fence_after();
-        const int valid = min(TK, len - j * TK);
-
-        // pass 1: running max of the scaled scores of this row
-        float mx = m_run;
-#pragma unroll 1
-        for (int c = 0; c < TK; c += 32) {
-            uint32_t v[32];
-            tmem_ld_x32(tS + c, v);
-            tmem_wait_ld();
+    } else {
+        // ------------------------------------------------ softmax warpgroups (warps 2..9)
+        const uint32_t g = static_cast<uint32_t>(warp - 2) >> 2;
+        const int q = warp & 3;
+        const int r = q * 32 + lane;  // query row within the tile == TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        const uint32_t tS = tmem + lane_base + g * 128;
+        const uint32_t tO = tmem + lane_base + 256 + g * 64;
+        float o[HD];
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (c + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]) * scale_log2);
-        }
-        const float alpha = fast_exp2(m_run - mx);  // exp2(-inf) = 0 on the first tile
-        // pass 2: p = exp2(s*scale - max), row sum, P tile in bf16 (128B-swizzled, K-major)
-        float rs = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < TK; c += 32) {
-            uint32_t v[32];
-            tmem_ld_x32(tS + c, v);
+        for (int d = 0; d < HD; ++d) o[d] = 0.f;
+        uint32_t it = 0;
+        bool ok = true, have_pend = false;
+        uint32_t pend_it = 0;
+        float pend_alpha = 0.f, pend_l = 1.f;
+        bool pend_last = false;
+        __nv_bfloat16 *pend_dst = nullptr;
+        bool pend_live = false;
+
+        auto consume = [&](uint32_t pit, float alpha, bool last, float l, __nv_bfloat16 *dst, bool live) -> bool {
+            if (!wait(&o_full[g], pit & 1)) return false;
+            if (!live) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_empty[g]);
+                return true;
+            }
+            tc_fence_after();
+            uint32_t v0[32], v1[32];
+            tmem_ld_x32(tO, v0);
+            tmem_ld_x32(tO + 32, v1);
             tmem_wait_ld();
-            float p[32];
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_empty[g]);
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                p[i] = (c + i < valid) ? fast_exp2(__uint_as_float(v[i]) * scale_log2 - mx) : 0.f;
-                rs += p[i];
+                o[i] = o[i] * alpha + __uint_as_float(v0[i]);
+                o[32 + i] = o[32 + i] * alpha + __uint_as_float(v1[i]);
             }
-            // columns c..c+31 = atom (c/64), 16-byte chunks (c%64)/8 .. +3 of row tid
-            uint8_t *row = sP + (c >> 6) * (TQ * 128) + tid * 128;
-            const int chunk0 = (c & 63) >> 3;
+            if (last) {
+                if (dst) {
+                    const float inv = 1.0f / l;
+                    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                uint4 w;
-                w.x = pack_bf16x2(p[u * 8 + 0], p[u * 8 + 1]);
-                w.y = pack_bf16x2(p[u * 8 + 2], p[u * 8 + 3]);
-                w.z = pack_bf16x2(p[u * 8 + 4], p[u * 8 + 5]);
-                w.w = pack_bf16x2(p[u * 8 + 6], p[u * 8 + 7]);
-                *reinterpret_cast<uint4 *>(row + (((chunk0 + u) ^ (tid & 7)) << 4)) = w;
+                    for (int x = 0; x < HD / 8; ++x) {
+                        uint4 wv;
+                        wv.x = pack_bf16x2(o[x * 8 + 0] * inv, o[x * 8 + 1] * inv);
+                        wv.y = pack_bf16x2(o[x * 8 + 2] * inv, o[x * 8 + 3] * inv);
+                        wv.z = pack_bf16x2(o[x * 8 + 4] * inv, o[x * 8 + 5] * inv);
+                        wv.w = pack_bf16x2(o[x * 8 + 6] * inv, o[x * 8 + 7] * inv);
+                        d4[x] = wv;
+                    }
+                }
+#pragma unroll
+                for (int d = 0; d < HD; ++d) o[d] = 0.f;
+            }
+            return true;
+        };
+
+        for (int k = static_cast<int>(g); k < nlist && ok; k += 2) {  // alternate units
+            if (*abort_flag) break;
+            const Unit w = unit_at(ulist, k);
+            float m_run = -INFINITY, l_run = 0.f;
+            __nv_bfloat16 *dst = nullptr;
+            if (w.q0 + r < w.len) {
+                const size_t row = static_cast<size_t>(w.start + w.q0 + r);
+                dst = head_major ? out + (static_cast<size_t>(w.head) * total_tokens + row) * HD
+                                 : out + row * dim + w.head * HD;
+            }
+            // A warp whose 32 query rows all lie past the sentence end does no softmax work:
+            // its P and O rows are never read back (each O row depends only on its P row).
+            const bool warp_live = w.q0 + q * 32 < w.len;
+            for (int j = 0; j < w.n_kv; ++j) {
+                if (!(ok = wait(&s_full[g], it & 1))) break;
+                tc_fence_after();
+                const int valid = min(TK, w.len - j * TK);
+                float mx = m_run, alpha = 1.f, rs0 = 0.f, rs1 = 0.f;
+                if (warp_live) {
+                    // pass 1: row max of the raw scores (four independent chains)
+                    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    for (int c = 0; c < valid; c += 32) {
+                        uint32_t v[32];
+                        tmem_ld_x32(tS + c, v);
+                        tmem_wait_ld();
+                        if (c + 32 <= valid) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (c + i < valid) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+                        }
+                    }
+                    mx = fmaxf(m_run, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale_log2);
+                    alpha = fast_exp2(m_run - mx);  // 0 on a unit's first item
+                    // pass 2: p = exp2(s * scale - max) in bf16, written back over S as P
+                    for (int c = 0; c < valid; c += 32) {
+                        uint32_t v[32];
+                        tmem_ld_x32(tS + c, v);
+                        tmem_wait_ld();
+                        uint32_t pk[16];
+                        if (c + 32 <= valid) {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float p0 = fast_exp2(fmaf(__uint_as_float(v[2 * i]), scale_log2, -mx));
+                                const float p1 = fast_exp2(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -mx));
+                                rs0 += p0;
+                                rs1 += p1;
+                                pk[i] = pack_bf16x2(p0, p1);
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float p0 = (c + 2 * i < valid) ? fast_exp2(fmaf(__uint_as_float(v[2 * i]), scale_log2, -mx)) : 0.f;
+                                const float p1 = (c + 2 * i + 1 < valid) ? fast_exp2(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -mx)) : 0.f;
+                                rs0 += p0;
+                                rs1 += p1;
+                                pk[i] = pack_bf16x2(p0, p1);
+                            }
+                        }
+                        tmem_st_x16(tS + (c >> 1), pk);  // P over the S columns already consumed
+                    }
+                }
+                if (warp_live) tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[g]);
+                l_run = l_run * alpha + (rs0 + rs1);
+                m_run = mx;
+                if (have_pend && !(ok = consume(pend_it, pend_alpha, pend_last, pend_l, pend_dst, pend_live))) break;
+                have_pend = true;
+                pend_it = it;
+                pend_alpha = alpha;
+                pend_last = j == w.n_kv - 1;
+                pend_l = l_run;
+                pend_dst = dst;
+                pend_live = warp_live;
+                ++it;
             }
         }
-        l_run = l_run * alpha + rs;
-        m_run = mx;
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t p_addr = smem_u32(sP), v_addr = smem_u32(sV);
-#pragma unroll
-            for (int ks = 0; ks < TK / 16; ++ks) {
-                const uint64_t ad = sdesc_sw128(p_addr + (ks >> 2) * (TQ * 128) + (ks & 3) * 32, 16, 1024);
-                const uint64_t bd = sdesc_sw128(v_addr + ks * 16 * 128, TK * 128, 1024);
-                umma_f16_ss(tmem + 128, ad, bd, idesc_o, ks != 0 ? 1u : 0u);
-            }
-            umma_commit(bar_o);
-            open_bar = bar_o;
-            open_par = par;
-        }
-        to = !mbar_wait(bar_o, par);
-        if (__syncthreads_or(to)) { aborted = true; break; }
-        open_bar = nullptr;
-        tc_fence_after();
-        // K/V buffers are free once PV has completed: fetch the next key tile.
-        if (tid == 0 && j + 1 < n_kv) {
-            mbar_arrive_expect_tx(bar_ld, 2 * TILE_BYTES);
-            tma_load_2d(sK, &tm_qkv, bar_ld, kcol, start + (j + 1) * TK);
-            tma_load_2d(sV, &tm_qkv, bar_ld, vcol, start + (j + 1) * TK);
-            ++arms;
-        }
-#pragma unroll
-        for (int c = 0; c < HD; c += 32) {
-            uint32_t v[32];
-            tmem_ld_x32(tO + c, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * alpha + __uint_as_float(v[i]);
-        }
+        if (ok && have_pend && !*abort_flag) (void)consume(pend_it, pend_alpha, pend_last, pend_l, pend_dst, pend_live);
     }
 
-    if (aborted) {
-        if (tid == 0) {
-            report(status, DEV_TIMEOUT);
-            // Loads and MMAs this CTA started must finish before smem / TMEM are released.
-            if (arms > landed && !mbar_wait(bar_ld, (arms - 1) & 1)) report(status, DEV_TIMEOUT);
-            if (open_bar && !mbar_wait(open_bar, open_par)) report(status, DEV_TIMEOUT);
-        }
-    } else if (q0 + tid < len) {
-        const float inv = 1.0f / l_run;
-        uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(start + q0 + tid) * dim + qcol);
-#pragma unroll
-        for (int u = 0; u < HD / 8; ++u) {
-            uint4 w;
-            w.x = pack_bf16x2(o[u * 8 + 0] * inv, o[u * 8 + 1] * inv);
-            w.y = pack_bf16x2(o[u * 8 + 2] * inv, o[u * 8 + 3] * inv);
-            w.z = pack_bf16x2(o[u * 8 + 4] * inv, o[u * 8 + 5] * inv);
-            w.w = pack_bf16x2(o[u * 8 + 6] * inv, o[u * 8 + 7] * inv);
-            dst[u] = w;
-        }
-    }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
@@ -238,16 +459,17 @@ __global__ void __launch_bounds__(128)
 
 }  // namespace
 
-cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, int batch,
-                                    int max_len, int heads, int head_dim, void *out,
-                                    int64_t total_tokens, cudaStream_t s, fe_status *st)
+cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, int batch, int max_len, int heads,
+                                    int head_dim, void *out, int64_t total_tokens, bool head_major, cudaStream_t s,
+                                    fe_status *st)
 {
     *st = FE_OK;
     if (batch == 0 || max_len == 0 || total_tokens == 0) return cudaSuccess;
     const int dim = heads * head_dim;
     CUtensorMap tm;
-    fe_status r = make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, total_tokens, 3 * (int64_t)dim,
-                               3 * (int64_t)dim, 128, HD);
+    fe_status r = head_major ? make_tmap_heads(&tm, qkv, 3 * static_cast<uint64_t>(heads), total_tokens, 128)
+                             : make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, total_tokens, 3 * (int64_t)dim,
+                                            3 * (int64_t)dim, 128, HD);
     if (r != FE_OK) {
         *st = r;
         return cudaSuccess;
@@ -262,10 +484,26 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
         configured[dev] = true;
     }
     const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
-    dim3 grid((max_len + TQ - 1) / TQ, batch, heads);
-    attn_varlen_tcgen05<<<grid, 128, SMEM_BYTES, s>>>(tm, cu_seqlens, dim,
-                                                      static_cast<__nv_bfloat16 *>(out), scale_log2,
-                                                      current_device_status_word());
+    const int qtiles = (max_len + TQ - 1) / TQ;
+    const int sms = current_sm_count();
+    // Sentence offsets are absolute rows of qkv, so a long batch runs as chunks over the
+    // same tensor map, each small enough that a CTA's unit list fits kMaxUnits.
+    int chunk = static_cast<int>(static_cast<int64_t>(kMaxUnits) * sms / (static_cast<int64_t>(qtiles) * heads));
+    if (chunk < 1) {
+        *st = fail(FE_ERR_UNSUPPORTED, "attention: too many heads x query tiles per sentence");
+        return cudaSuccess;
+    }
+    for (int b0 = 0; b0 < batch; b0 += chunk) {
+        const int nb = batch - b0 < chunk ? batch - b0 : chunk;
+        const int64_t units = static_cast<int64_t>(nb) * qtiles * heads;
+        const int grid = units < sms ? static_cast<int>(units) : sms;
+        attn_varlen_tcgen05<<<grid, kThreads, SMEM_BYTES, s>>>(tm, cu_seqlens + b0, nb, heads, qtiles,
+                                                               static_cast<__nv_bfloat16 *>(out), scale_log2,
+                                                               static_cast<int>(total_tokens), head_major ? 1 : 0,
+                                                               current_device_status_word());
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     return cudaGetLastError();
 }
 

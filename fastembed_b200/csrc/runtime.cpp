@@ -79,21 +79,27 @@ int current_sm_count()
     return g_sm_count[dev];
 }
 
+namespace {
+fe_status load_encode()
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return fail(FE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    return FE_OK;
+}
+}  // namespace
+
 fe_status make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes,
                        uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows, uint32_t box_cols,
                        bool swizzle128)
 {
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        if (!g_encode) {
-            void *fn = nullptr;
-            cudaDriverEntryPointQueryResult q;
-            if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-                q != cudaDriverEntryPointSuccess || !fn)
-                return fail(FE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-            g_encode = reinterpret_cast<EncodeTiledFn>(fn);
-        }
-    }
+    FE_TRY(load_encode());
     if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
         return fail(FE_ERR_INVALID_ARGUMENT, "TMA operand base must be 16-byte aligned");
     if ((ld * elem_bytes) % 16 != 0)
@@ -113,6 +119,22 @@ fe_status make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType d
                       static_cast<unsigned long long>(cols), box_rows, box_cols);
         return fail(FE_ERR_CUDA, buf);
     }
+    return FE_OK;
+}
+
+fe_status make_tmap_heads(CUtensorMap *map, const void *base, uint64_t heads, uint64_t rows, uint32_t box_rows)
+{
+    FE_TRY(load_encode());
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "TMA operand base must be 16-byte aligned");
+    cuuint64_t dims[3] = {64, rows, heads};
+    cuuint64_t strides[2] = {64 * 2, rows * 64 * 2};
+    cuuint32_t box[3] = {64, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FE_ERR_CUDA, "cuTensorMapEncodeTiled failed for a head-major tensor");
     return FE_OK;
 }
 

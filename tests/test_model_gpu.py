@@ -69,3 +69,48 @@ def test_rejects_too_long_and_bad_ids(cuda_dev):
     ok = eng.encode_host(np.full((1, 4), 200, np.int32), np.array([4], np.int32))
     assert abs(float(np.linalg.norm(ok)) - 1.0) < 1e-5
     eng.close()
+
+
+@pytest.mark.parametrize("name", ["bge-small", "bge-base", "bge-large"])
+def test_engine_matches_reference_golden(cuda_dev, name):
+    """Stored embeddings of the reference's own CPU forward (tests/golden/model_*.npz,
+    length-stratified sentences for the base and large shapes) on the same seeded
+    weights and ids; the sentences run inside their full batch on the GPU."""
+    import os
+    from fastembed_b200 import ops, workload as W
+    from tests.golden import gen_golden as G
+    gold = np.load(os.path.join(os.path.dirname(__file__), "golden", f"model_{name}.npz"))
+    shape = W.SHAPES[name]
+    weights = W.make_weights(shape)
+    assert G.weights_hash(weights) == str(gold["weights_sha256"]), "weight generator changed"
+    lengths = W.sample_lengths(shape)
+    ids, _ = W.sample_ids(shape, lengths)
+    assert G.sha(ids) == str(gold["ids_sha256"]), "id generator changed"
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(weights)
+    got = eng.encode_host(ids, lengths)
+    _check(got[gold["index"]], gold["embeddings"])
+    eng.close()
+
+
+def test_full_batch_properties_bge_large(cuda_dev):
+    """Size-independent checks at the benchmark's full size (256 sentences): unit
+    norms, run-to-run determinism, and bit-exact invariance to batch order and
+    composition (each sentence's result does not depend on its neighbours)."""
+    from fastembed_b200 import ops, workload as W
+    shape = W.SHAPES["bge-large"]
+    weights = W.make_weights(shape)
+    lengths = W.sample_lengths(shape)
+    ids, _ = W.sample_ids(shape, lengths)
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(weights)
+    a = eng.encode_host(ids, lengths)
+    b = eng.encode_host(ids, lengths)
+    assert np.array_equal(a, b)
+    assert np.abs(np.linalg.norm(a, axis=1) - 1).max() < 1e-5
+    perm = np.random.default_rng(0).permutation(lengths.size)
+    c = eng.encode_host(ids[perm], lengths[perm])
+    assert np.array_equal(c, a[perm])
+    d = eng.encode_host(ids[17:40], lengths[17:40])
+    assert np.array_equal(d, a[17:40])
+    eng.close()
