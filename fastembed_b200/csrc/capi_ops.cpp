@@ -21,6 +21,14 @@ inline fe_status done(cudaError_t e, const char *what) { return fe::check_cuda(e
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Row widths with a register-resident warp-per-row kernel (dim = 128 * v).
+bool supported_row_dim(int32_t dim)
+{
+    const int v = dim / 128;
+    return dim > 0 && dim % 128 == 0 && (v == 1 || v == 2 || v == 3 || v == 4 || v == 6 || v == 8 || v == 12 || v == 16);
+}
+
+
 }  // namespace
 
 extern "C" {
@@ -169,8 +177,6 @@ fe_status fe_attention_varlen_bf16(const void *qkv, const int32_t *cu_seqlens, i
     return done(e, "fe_attention_varlen_bf16");
 }
 
-static bool supported_row_dim(int32_t dim) { return dim > 0 && dim % 128 == 0 && (dim / 128) <= 16; }
-
 fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int32_t batch, int64_t total_tokens,
                              const float *word, const float *pos, const float *type, const float *gamma,
                              const float *beta, int32_t dim, int32_t vocab, int32_t max_pos, float eps, float *h32,
@@ -178,8 +184,7 @@ fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int3
 {
     if (batch < 0 || total_tokens < 0 || vocab <= 0 || max_pos <= 0)
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm: bad shape");
-    const int v = dim / 128;
-    if (!supported_row_dim(dim) || !(v == 2 || v == 3 || v == 4 || v == 6 || v == 8 || v == 12 || v == 16))
+    if (!supported_row_dim(dim) || dim == 128)
         return fail(FE_ERR_UNSUPPORTED, "fe_embed_layernorm: dim must be 256, 384, 512, 768, 1024, 1536 or 2048");
     if (total_tokens == 0) return FE_OK;
     if (batch == 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm: tokens without sentences");
@@ -190,14 +195,17 @@ fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int3
                 "fe_embed_layernorm");
 }
 
-fe_status fe_layernorm_dual(const float *x, const float *gamma, const float *beta, float *h32, void *h16,
-                            int64_t rows, int32_t dim, float eps, fe_stream_t stream)
+fe_status fe_layernorm_dual(const float *x, const float *residual, const float *gamma, const float *beta, float *h32,
+                            void *h16, int64_t rows, int32_t dim, float eps, fe_stream_t stream)
 {
     if (rows < 0 || dim <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_layernorm_dual: bad shape");
+    if (residual && !supported_row_dim(dim))
+        return fail(FE_ERR_UNSUPPORTED, "fe_layernorm_dual: the residual form needs dim in {128, 256, 384, 512, 768, "
+                                        "1024, 1536, 2048}");
     if (rows > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_layernorm_dual: too many rows");
     if (rows == 0) return FE_OK;
     if (!x || !gamma || !beta || !h32) return fail(FE_ERR_INVALID_ARGUMENT, "fe_layernorm_dual: null pointer");
-    return done(fe::launch_layernorm_dual(x, gamma, beta, h32, h16, rows, dim, eps,
+    return done(fe::launch_layernorm_dual(x, residual, gamma, beta, h32, h16, rows, dim, eps,
                                           reinterpret_cast<cudaStream_t>(stream)),
                 "fe_layernorm_dual");
 }

@@ -281,17 +281,18 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
             if (st != FE_OK) return st;
             FE_TRY_CUDA(err);
         }
-        FE_TRY(linear(e, s, attn, L.wo, L.bo, h32, y32, T, D, D, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32));
+        // out-proj + bias; the residual add is fused into the LayerNorm that follows
+        FE_TRY(linear(e, s, attn, L.wo, L.bo, nullptr, y32, T, D, D, FE_EPI_BIAS, FE_DTYPE_F32));
         {
             Scope sc(e, CAT_OTHER, s);
-            FE_TRY_CUDA(fe::launch_layernorm_dual(y32, L.ln1_g.as<float>(), L.ln1_b.as<float>(), h32, h16, T,
+            FE_TRY_CUDA(fe::launch_layernorm_dual(y32, h32, L.ln1_g.as<float>(), L.ln1_b.as<float>(), h32, h16, T,
                                                   static_cast<int>(D), c.layer_norm_eps, s));
         }
         FE_TRY(linear(e, s, h16, L.w1, L.b1, nullptr, ff, T, F, D, act, FE_DTYPE_BF16));
-        FE_TRY(linear(e, s, ff, L.w2, L.b2, h32, y32, T, D, F, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32));
+        FE_TRY(linear(e, s, ff, L.w2, L.b2, nullptr, y32, T, D, F, FE_EPI_BIAS, FE_DTYPE_F32));
         {
             Scope sc(e, CAT_OTHER, s);
-            FE_TRY_CUDA(fe::launch_layernorm_dual(y32, L.ln2_g.as<float>(), L.ln2_b.as<float>(), h32,
+            FE_TRY_CUDA(fe::launch_layernorm_dual(y32, h32, L.ln2_g.as<float>(), L.ln2_b.as<float>(), h32,
                                                   last ? nullptr : h16, T, static_cast<int>(D), c.layer_norm_eps, s));
         }
     }

@@ -7,24 +7,23 @@
 // softmax(Q K^T / sqrt(hd)) V with keys limited to the sentence, i.e. a key-padding
 // mask over a padded batch.
 //
-// Persistent, warp-specialised (one CTA per SM).  A work unit is (sentence, 128-row
-// query tile, head); an item is one 128-key tile of a unit.  All roles walk the same
-// unit sequence (blockIdx.x, +gridDim.x, ...) and skip query tiles past a sentence's end.
-//   warp 0     TMA producer: Q tile per unit into a 2-slot ring, K/V tiles per item into
-//              a 4-slot ring, read straight from the packed QKV buffer (no permute);
-//              tiles of the next units are prefetched into L2 ahead of the loads, so
-//              DRAM latency stays off the per-item chain.
-//   warp 1     TMEM owner + MMA issuer: S = Q K^T (M=128, N = keys rounded up to 16)
-//              into one of two TMEM S buffers; then, for the previous item, O = P V
-//              with P read from TMEM (A operand) and V as an MN-major smem operand.
-//   warps 2-9  two softmax warpgroups taking alternate units (ping-pong), each with
-//              its own TMEM S/P and O buffers: thread = query row; reads its S row
-//              (tcgen05.ld), masks keys past the sentence end, online max / sum, writes
-//              P (bf16) back over S (tcgen05.st); one item later folds O into fp32
-//              registers and, after a unit's last item, stores O / l.
-// One warpgroup's softmax overlaps the other's and the tensor core's S / PV.  Waits are
-// bounded; on timeout the CTA records FE_ERR_DEVICE_TIMEOUT, drains what it started
-// and exits.
+// Persistent and warp-specialised, two CTAs per SM, each an independent pipeline.  A
+// work unit is (sentence, 128-row query tile, head); an item is one 128-key tile of a
+// unit.  At start every CTA builds, in shared memory, the list of its units
+// (blockIdx.x, +gridDim.x, ...) whose query tile starts inside the sentence.
+//   warp 0     TMA producer: Q tile per unit and K/V tiles per item into 2-slot rings,
+//              straight from the QKV buffer (no permute); tiles of the next units are
+//              prefetched into L2 ahead of the loads.
+//   warp 1     TMEM owner + MMA issuer: S = Q K^T (M=128, N = keys rounded up to 16) into
+//              one of two 128-column TMEM slots; for the previous item, O = P V with P
+//              read from TMEM (A operand), V as an MN-major smem operand, O written into
+//              the upper 64 columns of P's slot.
+//   warps 2-5  softmax: thread = query row; reads its S row (tcgen05.ld), masks keys past
+//              the sentence end, online max / sum, writes P (bf16) back over the first 64
+//              columns (tcgen05.st); one item later folds O into fp32 registers and,
+//              after a unit's last item, stores O / l.
+// Waits are bounded; on timeout the CTA records FE_ERR_DEVICE_TIMEOUT, drains what it
+// started and exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -38,14 +37,16 @@ constexpr int HD = 64;
 constexpr int TQ = 128;
 constexpr int TK = 128;
 constexpr int Q_SLOTS = 2;
-constexpr int KV_SLOTS = 4;
-constexpr int kPrefetchItems = 8;  // key tiles the producer keeps requested into L2 ahead of its loads
+constexpr int KV_SLOTS = 2;
+constexpr int kPrefetchItems = 8;               // key tiles requested into L2 ahead of the loads
+constexpr int kMaxUnits = 1024;                 // per-CTA unit list capacity
+constexpr int kCtasPerSm = 2;
 constexpr uint32_t Q_BYTES = TQ * HD * 2;       // 16 KB
 constexpr uint32_t KV_BYTES = 2 * TK * HD * 2;  // K then V, 32 KB
-constexpr int kMaxUnits = 2048;  // per-CTA list of valid units, built at kernel start
-constexpr uint32_t SMEM_BYTES = 1024 + Q_SLOTS * Q_BYTES + KV_SLOTS * KV_BYTES + 512 + 12 * kMaxUnits + 64;
-constexpr uint32_t TMEM_COLS = 512;  // S/P of warpgroup g at g*128, its O at 256 + g*64
-constexpr int kThreads = 64 + 256;
+constexpr uint32_t BAR_BYTES = 256;
+constexpr uint32_t SMEM_BYTES = 1024 + Q_SLOTS * Q_BYTES + KV_SLOTS * KV_BYTES + BAR_BYTES + 12 * kMaxUnits + 64;
+constexpr uint32_t TMEM_COLS = 256;  // two slots: S [0,128) -> P [0,64) + O [64,128)
+constexpr int kThreads = 192;
 
 __device__ __forceinline__ float fast_exp2(float x)
 {
@@ -58,8 +59,8 @@ struct Unit {
     int start, len, q0, head, n_kv;
 };
 
-// A CTA's k-th valid unit, from the list built at kernel start: entry = {first row of
-// the sentence, sentence length, (head << 8) | query tile}.
+// A CTA's k-th valid unit: entry = {first row of the sentence, sentence length,
+// (head << 8) | query tile}.
 __device__ __forceinline__ Unit unit_at(const int3 *list, int k)
 {
     const int3 e = list[k];
@@ -72,7 +73,7 @@ __device__ __forceinline__ Unit unit_at(const int3 *list, int k)
     return w;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attn_varlen_tcgen05(const __grid_constant__ CUtensorMap tm_qkv, const int32_t *__restrict__ cu_seqlens,
                         int batch, int heads, int qtiles, __nv_bfloat16 *__restrict__ out, float scale_log2,
                         int total_tokens, int head_major, int *status)
@@ -82,20 +83,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *sQ = smem;
     uint8_t *sKV = sQ + Q_SLOTS * Q_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sKV + KV_SLOTS * KV_BYTES);
-    uint64_t *q_full = bars;                  // [2]
-    uint64_t *q_empty = q_full + Q_SLOTS;     // [2]
-    uint64_t *kv_full = q_empty + Q_SLOTS;    // [3]
-    uint64_t *kv_empty = kv_full + KV_SLOTS;  // [3]
-    uint64_t *s_full = kv_empty + KV_SLOTS;   // [2]
-    uint64_t *p_full = s_full + 2;            // [2]
-    uint64_t *s_free = p_full + 2;            // [2]
-    uint64_t *o_full = s_free + 2;            // [2]
-    uint64_t *o_empty = o_full + 2;           // [2]
-    uint64_t *probe = o_empty + 2;            // [1]
+    uint64_t *q_full = bars;                  // [Q_SLOTS]
+    uint64_t *q_empty = q_full + Q_SLOTS;     // [Q_SLOTS]
+    uint64_t *kv_full = q_empty + Q_SLOTS;    // [KV_SLOTS]
+    uint64_t *kv_empty = kv_full + KV_SLOTS;  // [KV_SLOTS]
+    uint64_t *s_full = kv_empty + KV_SLOTS;   // [2] S of a slot ready
+    uint64_t *p_full = s_full + 2;            // [2] P of a slot written
+    uint64_t *o_full = p_full + 2;            // [2] O of a slot ready
+    uint64_t *slot_free = o_full + 2;         // [2] O of a slot consumed
+    uint64_t *probe = slot_free + 2;          // [1]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(probe + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    int3 *ulist = reinterpret_cast<int3 *>(reinterpret_cast<uint8_t *>(bars) + 512);
-    int *warp_tot = reinterpret_cast<int *>(ulist + kMaxUnits);  // [10] + count
+    int3 *ulist = reinterpret_cast<int3 *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES);
+    int *warp_tot = reinterpret_cast<int *>(ulist + kMaxUnits);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -113,10 +113,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 4);  // one arrival per softmax warp
-            mbar_init(&s_free[i], 1);
+            mbar_init(&p_full[i], 4);     // one arrival per softmax warp
             mbar_init(&o_full[i], 1);
-            mbar_init(&o_empty[i], 4);
+            mbar_init(&slot_free[i], 4);  // one arrival per softmax warp
         }
         mbar_init(probe, 1);
         *abort_flag = 0;
@@ -127,18 +126,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
 
     // Unit u = blockIdx.x + i * gridDim.x is (sentence u / (H*QT), query tile (u / H) % QT,
     // head u % H); keep, in order, those whose query tile starts inside the sentence.
     {
         const int ncand = units > static_cast<int>(blockIdx.x) ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-        const int nwarps = blockDim.x >> 5;
+        constexpr int nwarps = kThreads / 32;
         int base = 0;
-        for (int c0 = 0; c0 < ncand; c0 += blockDim.x) {
+        for (int c0 = 0; c0 < ncand; c0 += kThreads) {
             const int ci = c0 + threadIdx.x;
             bool valid = false;
             int3 e = make_int3(0, 0, 0);
@@ -156,6 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) warp_tot[warp] = __popc(bal);
             __syncthreads();
             int off = base, total = 0;
+#pragma unroll
             for (int w2 = 0; w2 < nwarps; ++w2) {
                 if (w2 < warp) off += warp_tot[w2];
                 total += warp_tot[w2];
@@ -170,9 +166,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             base = 0;  // refuse the work rather than drop part of it
         }
         if (threadIdx.x == 0) warp_tot[nwarps] = base;
-        __syncthreads();
     }
-    const int nlist = warp_tot[blockDim.x >> 5];
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int nlist = warp_tot[kThreads / 32];
 
     auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
         if (mbar_wait(bar, parity)) return true;
@@ -239,66 +238,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
-            uint32_t qn = 0, kvn = 0, nunit = 0;
-            uint32_t itg[2] = {0, 0};  // items issued per softmax warpgroup
+            uint32_t qn = 0, kvn = 0, it = 0;
             bool issued = false, ok = true, have_pend = false;
-            uint32_t pend_g = 0, pend_it = 0, pend_ks = 0;
+            uint32_t pend_it = 0, pend_ks = 0;
             int pend_valid = 0;
-            // O[g] = P[g] V for warpgroup g's item `pit` (P from TMEM, V MN-major from smem)
-            auto issue_pv = [&](uint32_t g, uint32_t pit, uint32_t pks, int pvalid) -> bool {
-                if (!wait(&p_full[g], pit & 1)) return false;
-                if (!wait(&o_empty[g], (pit & 1) ^ 1)) return false;
+            // O(slot) = P(slot) V for item `pit` (P from TMEM, V MN-major from smem)
+            auto issue_pv = [&](uint32_t pit, uint32_t pks, int pvalid) -> bool {
+                const uint32_t b = pit & 1;
+                if (!wait(&p_full[b], (pit >> 1) & 1)) return false;
                 tc_fence_after();
-                const uint32_t v_addr = smem_u32(sKV + pks * KV_BYTES + KV_BYTES / 2);
+                const uint64_t v_desc = sdesc_sw128(smem_u32(sKV + pks * KV_BYTES + KV_BYTES / 2), TK * 128, 1024);
                 const int nks = (pvalid + 15) >> 4;
-                for (int ks = 0; ks < nks; ++ks)
-                    umma_f16_ts(tmem + 256 + g * 64, tmem + g * 128 + ks * 8,
-                                sdesc_sw128(v_addr + ks * 16 * 128, TK * 128, 1024), idesc_o, ks != 0 ? 1u : 0u);
-                umma_commit(&o_full[g]);
-                umma_commit(&s_free[g]);
+                for (int ks = 0; ks < nks; ++ks)  // each K step advances 16 key rows = 2048 bytes
+                    umma_f16_ts(tmem + b * 128 + 64, tmem + b * 128 + ks * 8, v_desc + static_cast<uint64_t>(ks * 128),
+                                idesc_o, ks != 0 ? 1u : 0u);
+                umma_commit(&o_full[b]);
                 umma_commit(&kv_empty[pks]);
                 return true;
             };
             for (int k = 0; k < nlist && ok && !*abort_flag; ++k) {
                 const Unit w = unit_at(ulist, k);
-                const uint32_t g = nunit++ & 1;
                 const int qs = qn % Q_SLOTS;
                 if (!(ok = wait(&q_full[qs], (qn / Q_SLOTS) & 1))) break;
-                const uint32_t q_addr = smem_u32(sQ + qs * Q_BYTES);
+                const uint64_t q_desc = sdesc_sw128(smem_u32(sQ + qs * Q_BYTES), 16, 1024);
                 for (int j = 0; j < w.n_kv; ++j) {
                     const uint32_t ks = kvn % KV_SLOTS;
-                    const uint32_t it = itg[g];
+                    const uint32_t b = it & 1;
                     if (!(ok = wait(&kv_full[ks], (kvn / KV_SLOTS) & 1))) break;
-                    // this warpgroup's previous item must finish PV before S reuses its TMEM
-                    if (have_pend && pend_g == g) {
-                        if (!(ok = issue_pv(pend_g, pend_it, pend_ks, pend_valid))) break;
-                        have_pend = false;
-                    }
-                    if (!(ok = wait(&s_free[g], (it & 1) ^ 1))) break;
+                    if (!(ok = wait(&slot_free[b], ((it >> 1) & 1) ^ 1))) break;
                     tc_fence_after();
                     const int valid = min(TK, w.len - j * TK);
                     const int n = min(TK, max(16, (valid + 15) & ~15));
                     const uint32_t idesc_s = idesc_bf16_f32(TQ, n, false, false);
-                    const uint32_t k_addr = smem_u32(sKV + ks * KV_BYTES);
+                    const uint64_t k_desc = sdesc_sw128(smem_u32(sKV + ks * KV_BYTES), 16, 1024);
 #pragma unroll
-                    for (int k = 0; k < HD / 16; ++k)
-                        umma_f16_ss(tmem + g * 128, sdesc_sw128(q_addr + k * 32, 16, 1024),
-                                    sdesc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
+                    for (int kk = 0; kk < HD / 16; ++kk)  // each K step advances 32 bytes inside the swizzle atom
+                        umma_f16_ss(tmem + b * 128, q_desc + static_cast<uint64_t>(kk * 2),
+                                    k_desc + static_cast<uint64_t>(kk * 2), idesc_s, kk != 0 ? 1u : 0u);
                     issued = true;
-                    umma_commit(&s_full[g]);
+                    umma_commit(&s_full[b]);
                     if (j == w.n_kv - 1) umma_commit(&q_empty[qs]);
-                    if (have_pend && !(ok = issue_pv(pend_g, pend_it, pend_ks, pend_valid))) break;
+                    if (have_pend && !(ok = issue_pv(pend_it, pend_ks, pend_valid))) break;
                     have_pend = true;
-                    pend_g = g;
                     pend_it = it;
                     pend_ks = ks;
                     pend_valid = valid;
-                    itg[g] = it + 1;
+                    ++it;
                     ++kvn;
                 }
                 ++qn;
             }
-            if (ok && have_pend && !*abort_flag) ok = issue_pv(pend_g, pend_it, pend_ks, pend_valid);
+            if (ok && have_pend && !*abort_flag) ok = issue_pv(pend_it, pend_ks, pend_valid);
             if (issued) {
                 // all MMAs issued by this thread retire before TMEM is released
                 umma_commit(probe);
@@ -306,13 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------ softmax warpgroups (warps 2..9)
-        const uint32_t g = static_cast<uint32_t>(warp - 2) >> 2;
+        // ------------------------------------------------ softmax warps 2..5
         const int q = warp & 3;
         const int r = q * 32 + lane;  // query row within the tile == TMEM lane
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        const uint32_t tS = tmem + lane_base + g * 128;
-        const uint32_t tO = tmem + lane_base + 256 + g * 64;
         float o[HD];
 #pragma unroll
         for (int d = 0; d < HD; ++d) o[d] = 0.f;
@@ -320,32 +307,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true, have_pend = false;
         uint32_t pend_it = 0;
         float pend_alpha = 0.f, pend_l = 1.f;
-        bool pend_last = false;
+        bool pend_last = false, pend_live = false;
         __nv_bfloat16 *pend_dst = nullptr;
-        bool pend_live = false;
 
         auto consume = [&](uint32_t pit, float alpha, bool last, float l, __nv_bfloat16 *dst, bool live) -> bool {
-            if (!wait(&o_full[g], pit & 1)) return false;
-            if (!live) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&o_empty[g]);
-                return true;
+            const uint32_t b = pit & 1;
+            if (!wait(&o_full[b], (pit >> 1) & 1)) return false;
+            if (live) {
+                tc_fence_after();
+                uint32_t v0[32], v1[32];
+                const uint32_t tO = tmem + lane_base + b * 128 + 64;
+                tmem_ld_x32(tO, v0);
+                tmem_ld_x32(tO + 32, v1);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    o[i] = o[i] * alpha + __uint_as_float(v0[i]);
+                    o[32 + i] = o[32 + i] * alpha + __uint_as_float(v1[i]);
+                }
             }
-            tc_fence_after();
-            uint32_t v0[32], v1[32];
-            tmem_ld_x32(tO, v0);
-            tmem_ld_x32(tO + 32, v1);
-            tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&o_empty[g]);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                o[i] = o[i] * alpha + __uint_as_float(v0[i]);
-                o[32 + i] = o[32 + i] * alpha + __uint_as_float(v1[i]);
-            }
-            if (last) {
+            if (lane == 0) mbar_arrive(&slot_free[b]);
+            if (live && last) {
                 if (dst) {
                     const float inv = 1.0f / l;
                     uint4 *d4 = reinterpret_cast<uint4 *>(dst);
@@ -365,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             return true;
         };
 
-        for (int k = static_cast<int>(g); k < nlist && ok; k += 2) {  // alternate units
+        for (int k = 0; k < nlist && ok; ++k) {
             if (*abort_flag) break;
             const Unit w = unit_at(ulist, k);
             float m_run = -INFINITY, l_run = 0.f;
@@ -379,9 +363,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // its P and O rows are never read back (each O row depends only on its P row).
             const bool warp_live = w.q0 + q * 32 < w.len;
             for (int j = 0; j < w.n_kv; ++j) {
-                if (!(ok = wait(&s_full[g], it & 1))) break;
+                const uint32_t b = it & 1;
+                if (!(ok = wait(&s_full[b], (it >> 1) & 1))) break;
                 tc_fence_after();
                 const int valid = min(TK, w.len - j * TK);
+                const uint32_t tS = tmem + lane_base + b * 128;
                 float mx = m_run, alpha = 1.f, rs0 = 0.f, rs1 = 0.f;
                 if (warp_live) {
                     // pass 1: row max of the raw scores (four independent chains)
@@ -428,11 +414,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         tmem_st_x16(tS + (c >> 1), pk);  // P over the S columns already consumed
                     }
+                    tmem_wait_st();
                 }
-                if (warp_live) tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&p_full[g]);
+                if (lane == 0) mbar_arrive(&p_full[b]);
                 l_run = l_run * alpha + (rs0 + rs1);
                 m_run = mx;
                 if (have_pend && !(ok = consume(pend_it, pend_alpha, pend_last, pend_l, pend_dst, pend_live))) break;
@@ -446,7 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++it;
             }
         }
-        if (ok && have_pend && !*abort_flag) (void)consume(pend_it, pend_alpha, pend_last, pend_l, pend_dst, pend_live);
+        if (ok && have_pend && !*abort_flag)
+            (void)consume(pend_it, pend_alpha, pend_last, pend_l, pend_dst, pend_live);
     }
 
     tc_fence_before();
@@ -485,10 +472,10 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
     }
     const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
     const int qtiles = (max_len + TQ - 1) / TQ;
-    const int sms = current_sm_count();
+    const int ctas = kCtasPerSm * current_sm_count();
     // Sentence offsets are absolute rows of qkv, so a long batch runs as chunks over the
     // same tensor map, each small enough that a CTA's unit list fits kMaxUnits.
-    int chunk = static_cast<int>(static_cast<int64_t>(kMaxUnits) * sms / (static_cast<int64_t>(qtiles) * heads));
+    const int chunk = static_cast<int>(static_cast<int64_t>(kMaxUnits) * ctas / (static_cast<int64_t>(qtiles) * heads));
     if (chunk < 1) {
         *st = fail(FE_ERR_UNSUPPORTED, "attention: too many heads x query tiles per sentence");
         return cudaSuccess;
@@ -496,7 +483,7 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
     for (int b0 = 0; b0 < batch; b0 += chunk) {
         const int nb = batch - b0 < chunk ? batch - b0 : chunk;
         const int64_t units = static_cast<int64_t>(nb) * qtiles * heads;
-        const int grid = units < sms ? static_cast<int>(units) : sms;
+        const int grid = units < ctas ? static_cast<int>(units) : ctas;
         attn_varlen_tcgen05<<<grid, kThreads, SMEM_BYTES, s>>>(tm, cu_seqlens + b0, nb, heads, qtiles,
                                                                static_cast<__nv_bfloat16 *>(out), scale_log2,
                                                                static_cast<int>(total_tokens), head_major ? 1 : 0,
@@ -504,7 +491,7 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    return cudaGetLastError();
+    return cudaSuccess;
 }
 
 }  // namespace fe

@@ -97,10 +97,14 @@ __global__ void __launch_bounds__(256)
     ln_store<VPT>(x, g, b, o32, o16, dim, eps, lane);
 }
 
+// h = LayerNorm(y [+ res]) with fp32 and bf16 outputs.  With `res`, the sum y + res is
+// formed here (y already holds x W^T + b), the order of the reference's residual add
+// (src/sentence_transformers_impl.cpp:255-263, :429-436).  h32 may alias res: every
+// element is read before the thread that owns it writes it.
 template <int VPT>
 __global__ void __launch_bounds__(256)
-    ln_dual(const float *__restrict__ in, const float *__restrict__ g, const float *__restrict__ b,
-            float *__restrict__ h32, __nv_bfloat16 *__restrict__ h16, int64_t rows, float eps)
+    ln_dual(const float *__restrict__ in, const float *res, const float *__restrict__ g, const float *__restrict__ b,
+            float *h32, __nv_bfloat16 *__restrict__ h16, int64_t rows, float eps)
 {
     constexpr int dim = 128 * VPT;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -110,6 +114,17 @@ __global__ void __launch_bounds__(256)
     float4 x[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) x[i] = *reinterpret_cast<const float4 *>(src + (i * 32 + lane) * 4);
+    if (res) {
+        const float *rr = res + r * dim;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const float4 a = *reinterpret_cast<const float4 *>(rr + (i * 32 + lane) * 4);
+            x[i].x += a.x;
+            x[i].y += a.y;
+            x[i].z += a.z;
+            x[i].w += a.w;
+        }
+    }
     ln_store<VPT>(x, g, b, h32 + r * dim, h16 ? h16 + r * dim : nullptr, dim, eps, lane);
 }
 
@@ -147,7 +162,7 @@ __global__ void __launch_bounds__(256)
                float *__restrict__ h32, __nv_bfloat16 *__restrict__ h16, int64_t dim, float eps)
 {
     __shared__ float red[33];
-    const float *x = in + static_cast<int64_t>(blockIdx.x) * dim;
+    const float *x = in + static_cast<int64_t>(blockIdx.x) * dim;  // (no residual form: dims the fast path lacks)
     float s = 0.f;
     for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) s += x[i];
     const float mean = block_sum(s, red) / static_cast<float>(dim);
@@ -267,18 +282,20 @@ cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int ba
     return cudaGetLastError();
 }
 
-cudaError_t launch_layernorm_dual(const float *x, const float *g, const float *b, float *h32, void *h16,
-                                  int64_t rows, int dim, float eps, cudaStream_t s)
+cudaError_t launch_layernorm_dual(const float *x, const float *res, const float *g, const float *b, float *h32,
+                                  void *h16, int64_t rows, int dim, float eps, cudaStream_t s)
 {
     if (rows == 0) return cudaSuccess;
     auto *o16 = static_cast<__nv_bfloat16 *>(h16);
     const unsigned grid = grid_for(rows, 8);
     switch (dim) {
 #define FE_LN(V) \
-    case 128 * V: ln_dual<V><<<grid, 256, 0, s>>>(x, g, b, h32, o16, rows, eps); break;
+    case 128 * V: ln_dual<V><<<grid, 256, 0, s>>>(x, res, g, b, h32, o16, rows, eps); break;
         FE_LN(1) FE_LN(2) FE_LN(3) FE_LN(4) FE_LN(6) FE_LN(8) FE_LN(12) FE_LN(16)
 #undef FE_LN
-        default: ln_generic<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, g, b, h32, o16, dim, eps);
+        default:
+            if (res) return cudaErrorInvalidValue;
+            ln_generic<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, g, b, h32, o16, dim, eps);
     }
     return cudaGetLastError();
 }

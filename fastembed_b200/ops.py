@@ -118,12 +118,12 @@ def embed_layernorm(ids, cu_seqlens, word, pos, type_, gamma, beta, eps):
     return h32, h16
 
 
-def layernorm_dual(x, gamma, beta, eps):
-    _cuda(x, gamma, beta)
+def layernorm_dual(x, gamma, beta, eps, residual=None):
+    _cuda(x, gamma, beta, residual)
     rows, D = x.shape
     h32 = torch.empty_like(x)
     h16 = torch.empty(rows, D, dtype=torch.bfloat16, device=x.device)
-    call("fe_layernorm_dual", _p(x), _p(gamma), _p(beta), _p(h32), _p(h16), rows, D, eps, _s(x))
+    call("fe_layernorm_dual", _p(x), _p(residual), _p(gamma), _p(beta), _p(h32), _p(h16), rows, D, eps, _s(x))
     return h32, h16
 
 

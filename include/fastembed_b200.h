@@ -148,10 +148,11 @@ fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int3
                              const float *type, const float *gamma, const float *beta,
                              int32_t dim, int32_t vocab, int32_t max_pos, float eps,
                              float *h32, void *h16, fe_stream_t stream);
-/* Row LayerNorm writing fp32 and (when h16 != NULL) bf16 copies; the post-residual
- * norms of src/sentence_transformers_impl.cpp:266 and :437. */
-fe_status fe_layernorm_dual(const float *x, const float *gamma, const float *beta, float *h32,
-                            void *h16, int64_t rows, int32_t dim, float eps, fe_stream_t stream);
+/* h = LayerNorm(x + residual) (residual may be NULL) writing fp32 and (when
+ * h16 != NULL) bf16 copies: the residual add and post-residual norms of
+ * src/sentence_transformers_impl.cpp:255-266 and :429-437.  h32 may alias residual. */
+fe_status fe_layernorm_dual(const float *x, const float *residual, const float *gamma, const float *beta,
+                            float *h32, void *h16, int64_t rows, int32_t dim, float eps, fe_stream_t stream);
 /* Per-sentence pooling + L2 normalisation of packed hidden states h [total, dim]
  * into out [batch, dim].  Replaces src/sentence_transformers_impl.cpp:289-341. */
 fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, int32_t dim,

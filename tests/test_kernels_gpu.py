@@ -28,14 +28,21 @@ LINEAR_SHAPES = [
     (129, 1024, 4096),  # FFN2 shape (long K)
     (64, 512, 72),      # K not a multiple of 64 (TMA zero fill)
     (96, 1000, 64),     # N not a multiple of 64 (clipped store)
+    (700, 1024, 4096),  # 2-CTA pair tiles, ragged last pair
+    (4097, 256, 64),    # 2-CTA, many m tiles, peer half of the last tile out of range
+    (520, 768, 72),     # 2-CTA with a zero-filled K tail
 ]
 
 
+@pytest.mark.parametrize("pair", ["1", "0"])
 @pytest.mark.parametrize("m,n,k", LINEAR_SHAPES)
 @pytest.mark.parametrize("epi,out", [("none", "f32"), ("bias", "bf16"), ("bias_gelu", "bf16"),
                                      ("bias_residual", "f32")])
-def test_linear_bf16(cuda_dev, m, n, k, epi, out):
+def test_linear_bf16(cuda_dev, monkeypatch, m, n, k, epi, out, pair):
+    """Both linear kernels: the 2-CTA pair kernel (default for m >= 512 and n % 256 == 0)
+    and the 1-CTA kernel (FE_LINEAR_PAIR=0)."""
     from fastembed_b200 import ops
+    monkeypatch.setenv("FE_LINEAR_PAIR", pair)
     g = torch.Generator(device=cuda_dev).manual_seed(m * 7 + n + k)
     x = torch.randn(m, k, device=cuda_dev, generator=g).to(torch.bfloat16)
     w = (torch.randn(n, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
@@ -82,7 +89,7 @@ def test_linear_deterministic_and_row_independent(cuda_dev):
     y2 = ops.linear_bf16(x, w, b, None, "bias", "bf16")
     y3 = ops.linear_bf16(x[300:437].contiguous(), w, b, None, "bias", "bf16")
     assert torch.equal(y1, y2)
-    assert torch.equal(y1[300:437], y3)
+    assert torch.equal(y1[300:437], y3)  # 1-CTA kernel for the block, pair kernel for the batch
 
 
 # ------------------------------------------------------------ varlen attention
@@ -164,6 +171,12 @@ def test_layernorm_dual(cuda_dev):
         ref = torch.nn.functional.layer_norm(x, (D,), gam, bet, 1e-12)
         assert float((h32 - ref).abs().max()) < 1e-4
         assert torch.equal(h16, h32.to(torch.bfloat16))
+        if D in (512, 768, 1024):  # residual form: LN(x + res), sum formed in the kernel
+            res = torch.randn(777, D, device=cuda_dev, generator=g)
+            h32r, h16r = ops.layernorm_dual(x, gam, bet, 1e-12, residual=res)
+            refr = torch.nn.functional.layer_norm(x + res, (D,), gam, bet, 1e-12)
+            assert float((h32r - refr).abs().max()) < 1e-4
+            assert torch.equal(h16r, h32r.to(torch.bfloat16))
 
 
 @pytest.mark.parametrize("mode", ["cls", "mean", "last"])
