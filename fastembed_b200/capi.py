@@ -58,6 +58,7 @@ _SIGS = {
     "fe_softmax_scores_inplace_f32": ([vp, i64, i64, vp], C.c_int),
     "fe_mha_f32_workspace_bytes": ([i64, i64, i64], sz),
     "fe_mha_f32": ([vp] * 8 + [i64, i64, i64, vp, sz, vp], C.c_int),
+    "fe_mha_f32_noalloc": ([vp] * 8 + [i64, i64, i64, vp], C.c_int),
     "fe_linear_bf16": ([vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, C.c_int, vp], C.c_int),
     "fe_attention_varlen_bf16": ([vp, vp, i32, i32, i32, i32, vp, i64, vp], C.c_int),
     "fe_embed_layernorm": ([vp, vp, i32, i64, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, vp], C.c_int),

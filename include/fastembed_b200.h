@@ -116,6 +116,16 @@ fe_status fe_mha_f32(const float *x, const float *wq, const float *wk, const flo
                      const float *bq, const float *bk, const float *bv, float *out,
                      int64_t seq_len, int64_t dim, int64_t heads, void *workspace,
                      size_t workspace_bytes, fe_stream_t stream);
+/* fe_mha_f32 without a workspace argument and without allocating: Q, K and V live in
+ * a fixed 3 MiB scratch array inside the library (one per device, kept until process
+ * exit), for callers that cannot allocate device memory on demand.  No counterpart in
+ * the reference (its attention op allocates per call).  Requires seq_len * dim <=
+ * 262144 (FE_ERR_UNSUPPORTED otherwise).  All calls on a device share the scratch, so
+ * calls whose GPU work overlaps race; order them on one stream.  The first call on a
+ * device looks up the scratch address and should precede any stream capture. */
+fe_status fe_mha_f32_noalloc(const float *x, const float *wq, const float *wk, const float *wv,
+                             const float *bq, const float *bk, const float *bv, float *out,
+                             int64_t seq_len, int64_t dim, int64_t heads, fe_stream_t stream);
 
 /* ----------------------------------- BF16 tensor-core hot-path ops -----
  * tcgen05 (TMEM accumulator, TMA-fed) kernels of the model pipeline. */
