@@ -1,0 +1,334 @@
+// sentence_transformers.cpp — the drop-in SentenceTransformer over the device engine.
+//
+// Construction mirrors SentenceTransformerImpl's (src/sentence_transformers_impl.cpp:46-98):
+// config.json, a WordPiece vocabulary (vocab.txt) and model.safetensors from one model
+// directory.  encode / encode_batch tokenise on the host (BGE WordPiece, then [CLS]=101
+// in front and [SEP]=102 behind, :11-27) and run every sentence of the batch in one
+// packed device pass per GPU instead of a per-text loop (:359-365).  With FE_DEVICES
+// listing several GPUs, a batch is sorted by length and cut into contiguous slices of
+// equal algorithmic work, one per GPU, each run by its own host thread; there is no
+// device-to-device traffic.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cctype>
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <iostream>
+#include <mutex>
+#include <numeric>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "fastembed_b200.h"
+#include "json_min.h"
+#include "sentence_transformers.h"
+
+namespace {
+
+void check(fe_status st, const std::string &where)
+{
+    if (st == FE_OK) return;
+    const std::string msg = where + ": " + fe_last_error_message();
+    if (st == FE_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+    throw std::runtime_error(msg);
+}
+
+// BGE WordPiece tokenizer with the reference's behaviour (src/tokenizer.cpp:9-160):
+// whitespace separates words; every non-ASCII UTF-8 character is a word of its own;
+// ASCII letters and digits accumulate lower-cased; any other ASCII byte is a word of
+// its own; each word is looked up whole, else split greedily into the longest known
+// prefix then "##"-continuations, and becomes a single [UNK] if a piece is missing.
+class WordPiece {
+public:
+    explicit WordPiece(const std::string &vocab_file)
+    {
+        std::ifstream f(vocab_file);
+        if (!f.is_open()) throw std::runtime_error("cannot open vocabulary file: " + vocab_file);
+        std::string line;
+        int id = 0;
+        while (std::getline(f, line)) vocab_[line] = id++;
+        auto it = vocab_.find("[UNK]");
+        if (it == vocab_.end()) throw std::runtime_error("vocabulary has no [UNK] token");
+        unk_ = it->second;
+    }
+
+    std::vector<int32_t> ids(const std::string &text) const
+    {
+        std::vector<int32_t> out;
+        for (const std::string &w : words(text)) pieces(w, out);
+        return out;
+    }
+
+private:
+    std::unordered_map<std::string, int32_t> vocab_;
+    int32_t unk_ = 0;
+
+    static std::vector<std::string> words(const std::string &text)
+    {
+        std::vector<std::string> out;
+        std::string cur;
+        auto flush = [&] {
+            if (!cur.empty()) {
+                out.push_back(cur);
+                cur.clear();
+            }
+        };
+        size_t i = 0;
+        while (i < text.size()) {
+            const unsigned char c = static_cast<unsigned char>(text[i]);
+            if (std::isspace(c)) {
+                flush();
+                ++i;
+                continue;
+            }
+            if (c & 0x80) {
+                size_t n = 0;
+                if ((c & 0xE0) == 0xC0) n = 2;
+                else if ((c & 0xF0) == 0xE0) n = 3;
+                else if ((c & 0xF8) == 0xF0) n = 4;
+                if (n == 0 || i + n > text.size()) {  // stray or truncated byte
+                    out.push_back("[UNK]");
+                    ++i;
+                    continue;
+                }
+                flush();
+                out.push_back(text.substr(i, n));
+                i += n;
+                continue;
+            }
+            if (std::isalnum(c)) {
+                cur.push_back(static_cast<char>(std::tolower(c)));
+            } else {
+                flush();
+                out.push_back(std::string(1, static_cast<char>(c)));
+            }
+            ++i;
+        }
+        flush();
+        return out;
+    }
+
+    void pieces(const std::string &w, std::vector<int32_t> &out) const
+    {
+        auto whole = vocab_.find(w);
+        if (whole != vocab_.end()) {
+            out.push_back(whole->second);
+            return;
+        }
+        std::vector<int32_t> found;
+        size_t start = 0;
+        while (start < w.size()) {
+            bool hit = false;
+            for (size_t end = w.size(); end > start; --end) {
+                const std::string sub = (start > 0 ? "##" : "") + w.substr(start, end - start);
+                auto it = vocab_.find(sub);
+                if (it != vocab_.end()) {
+                    found.push_back(it->second);
+                    start = end;
+                    hit = true;
+                    break;
+                }
+            }
+            if (!hit) {
+                out.push_back(unk_);
+                return;
+            }
+        }
+        out.insert(out.end(), found.begin(), found.end());
+    }
+};
+
+std::string read_file(const std::string &path)
+{
+    std::ifstream f(path, std::ios::binary);
+    if (!f.is_open()) throw std::runtime_error("cannot open " + path);
+    std::stringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+int cfg_int(const fe::json::Value &cfg, const char *key, int fallback)
+{
+    return cfg.has(key) ? static_cast<int>(cfg.at(key).as_number()) : fallback;
+}
+
+}  // namespace
+
+class SentenceTransformerImpl {
+public:
+    explicit SentenceTransformerImpl(const std::string &model_path)
+    {
+        const fe::json::Value cfg = fe::json::parse(read_file(model_path + "/config.json"));
+        std::string type = "bge";
+        if (cfg.has("model_type")) type = cfg.at("model_type").as_string();
+        else if (cfg.has("model") && cfg.at("model").has("model_type")) type = cfg.at("model").at("model_type").as_string();
+        if (type != "bge" && type != "bert")
+            throw std::runtime_error("model type '" + type +
+                                     "' needs the XLM-R SentencePiece tokenizer, which this build does not include");
+        fe_encoder_config c{};
+        c.vocab_size = cfg_int(cfg, "vocab_size", 0);
+        c.hidden = cfg_int(cfg, "hidden_size", 0);
+        c.layers = cfg_int(cfg, "num_hidden_layers", 0);
+        c.heads = cfg_int(cfg, "num_attention_heads", 0);
+        c.intermediate = cfg_int(cfg, "intermediate_size", 0);
+        c.max_position = cfg_int(cfg, "max_position_embeddings", 512);
+        c.type_vocab = cfg_int(cfg, "type_vocab_size", 2);
+        c.layer_norm_eps = cfg.has("layer_norm_eps") ? static_cast<float>(cfg.at("layer_norm_eps").as_number()) : 1e-12f;
+        const std::string act = cfg.has("hidden_act") ? cfg.at("hidden_act").as_string() : "gelu";
+        if (act == "gelu") c.activation = FE_ACT_GELU;
+        else if (act == "relu") c.activation = FE_ACT_RELU;
+        else if (act == "swish") c.activation = FE_ACT_SWISH;
+        else throw std::runtime_error("Unsupported activation function");  // (:413-421)
+        c.pooling = FE_POOL_CLS;
+        cfg_ = c;
+        tokenizer_.reset(new WordPiece(model_path + "/vocab.txt"));
+
+        for (int dev : devices()) {
+            check(cudaSetDevice(dev) == cudaSuccess ? FE_OK : FE_ERR_CUDA, "cudaSetDevice");
+            fe_engine *e = nullptr;
+            check(fe_engine_create(&cfg_, dev, &e), "fe_engine_create");
+            engines_.push_back(e);
+            fe_status st = fe_engine_load_safetensors(e, (model_path + "/model.safetensors").c_str());
+            if (st == FE_OK && fe_engine_missing_weights(e) != 0)
+                throw std::runtime_error("model.safetensors lacks some encoder weights");
+            check(st, "load model.safetensors");
+        }
+    }
+
+    ~SentenceTransformerImpl()
+    {
+        for (fe_engine *e : engines_) fe_engine_destroy(e);
+    }
+
+    size_t dim() const { return static_cast<size_t>(cfg_.hidden); }
+
+    std::vector<int32_t> tokenize(const std::string &text) const
+    {
+        std::vector<int32_t> ids = tokenizer_->ids(text);
+        ids.insert(ids.begin(), 101);
+        ids.push_back(102);
+        return ids;
+    }
+
+    std::vector<std::vector<float>> run(const std::vector<std::vector<int32_t>> &seqs)
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        const int B = static_cast<int>(seqs.size());
+        std::vector<std::vector<float>> out(B, std::vector<float>(dim()));
+        if (B == 0) return out;
+        for (const auto &s : seqs)
+            if (static_cast<int>(s.size()) > cfg_.max_position)
+                throw std::runtime_error("sequence longer than the position embedding table");  // (:132-136)
+        // longest first, so that contiguous slices are balanced by fe_plan_shards
+        std::vector<int> order(B);
+        std::iota(order.begin(), order.end(), 0);
+        std::stable_sort(order.begin(), order.end(),
+                         [&](int a, int b) { return seqs[a].size() > seqs[b].size(); });
+        std::vector<int32_t> lens(B);
+        int stride = 1;
+        for (int i = 0; i < B; ++i) {
+            lens[i] = static_cast<int32_t>(seqs[order[i]].size());
+            stride = std::max(stride, static_cast<int>(lens[i]));
+        }
+        const int parts = std::min<int>(static_cast<int>(engines_.size()), B);
+        std::vector<int32_t> cuts(std::max(parts - 1, 1));
+        check(fe_plan_shards(&cfg_, lens.data(), B, parts, cuts.data()), "fe_plan_shards");
+        std::vector<int> bounds{0};
+        for (int p = 0; p + 1 < parts; ++p) bounds.push_back(cuts[p]);
+        bounds.push_back(B);
+
+        std::vector<fe_status> status(parts, FE_OK);
+        std::vector<std::string> errors(parts);
+        auto work = [&](int p) {
+            const int b0 = bounds[p], nb = bounds[p + 1] - b0;
+            if (nb == 0) return;
+            std::vector<int32_t> ids(static_cast<size_t>(nb) * stride, 0), sl(nb);
+            for (int i = 0; i < nb; ++i) {
+                const auto &s = seqs[order[b0 + i]];
+                std::copy(s.begin(), s.end(), ids.begin() + static_cast<size_t>(i) * stride);
+                sl[i] = static_cast<int32_t>(s.size());
+            }
+            std::vector<float> emb(static_cast<size_t>(nb) * dim());
+            status[p] = fe_engine_encode_host(engines_[p], ids.data(), sl.data(), nb, stride, emb.data());
+            if (status[p] != FE_OK) {
+                errors[p] = fe_last_error_message();
+                return;
+            }
+            for (int i = 0; i < nb; ++i)
+                std::copy(emb.begin() + static_cast<size_t>(i) * dim(), emb.begin() + static_cast<size_t>(i + 1) * dim(),
+                          out[order[b0 + i]].begin());
+        };
+        if (parts == 1) {
+            work(0);
+        } else {
+            std::vector<std::thread> pool;
+            for (int p = 0; p < parts; ++p) pool.emplace_back(work, p);
+            for (auto &t : pool) t.join();
+        }
+        for (int p = 0; p < parts; ++p)
+            if (status[p] != FE_OK) {
+                const std::string msg = "encode on GPU slice " + std::to_string(p) + ": " + errors[p];
+                if (status[p] == FE_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+                throw std::runtime_error(msg);
+            }
+        return out;
+    }
+
+private:
+    fe_encoder_config cfg_{};
+    std::unique_ptr<WordPiece> tokenizer_;
+    std::vector<fe_engine *> engines_;
+    std::mutex mu_;
+
+    static std::vector<int> devices()
+    {
+        std::vector<int> out;
+        if (const char *env = std::getenv("FE_DEVICES")) {
+            std::stringstream ss(env);
+            std::string tok;
+            while (std::getline(ss, tok, ','))
+                if (!tok.empty()) out.push_back(std::stoi(tok));
+        }
+        if (out.empty()) out.push_back(0);
+        return out;
+    }
+};
+
+SentenceTransformer::SentenceTransformer(const std::string &model_path) : impl(new SentenceTransformerImpl(model_path)) {}
+SentenceTransformer::~SentenceTransformer() = default;
+SentenceTransformer::SentenceTransformer(SentenceTransformer &&) noexcept = default;
+SentenceTransformer &SentenceTransformer::operator=(SentenceTransformer &&) noexcept = default;
+
+std::vector<float> SentenceTransformer::encode(const std::string &text)
+{
+    std::vector<int32_t> ids = impl->tokenize(text);
+    if (const char *p = std::getenv("FE_PRINT_TOKENS"); p && p[0] == '1') {  // (:350-354)
+        std::cout << "tokens: " << std::endl;
+        for (int32_t t : ids) std::cout << t << " ";
+        std::cout << std::endl;
+    }
+    return impl->run({ids})[0];
+}
+
+std::vector<std::vector<float>> SentenceTransformer::encode_batch(const std::vector<std::string> &texts)
+{
+    std::vector<std::vector<int32_t>> seqs;
+    seqs.reserve(texts.size());
+    for (const auto &t : texts) seqs.push_back(impl->tokenize(t));
+    return impl->run(seqs);
+}
+
+std::vector<std::vector<float>> SentenceTransformer::encode_ids(const std::vector<std::vector<int32_t>> &ids)
+{
+    return impl->run(ids);
+}
+
+size_t SentenceTransformer::get_embedding_dimension() const { return impl->dim(); }
+
+std::vector<int32_t> SentenceTransformer::tokenize(const std::string &text) const { return impl->tokenize(text); }

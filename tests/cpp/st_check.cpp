@@ -1,0 +1,50 @@
+// st_check.cpp — drives the drop-in SentenceTransformer the way the reference's CLI and
+// server do (construct from a model directory, encode / encode_batch), for the
+// model-level test in tests/test_dropin_gpu.py.
+//
+//   st_check <model_dir> <texts_file> <out_prefix>
+// reads one text per line and writes <out_prefix>.ids (per text: int32 count, then the
+// ids), <out_prefix>.batch (float32 [n, dim] from encode_batch) and <out_prefix>.single
+// (float32 [n, dim] from encode, one text at a time).
+#include <cstdint>
+#include <cstdio>
+#include <fstream>
+#include <iostream>
+#include <string>
+#include <vector>
+
+#include "sentence_transformers.h"
+
+int main(int argc, char **argv)
+{
+    if (argc != 4) {
+        std::fprintf(stderr, "usage: st_check <model_dir> <texts_file> <out_prefix>\n");
+        return 2;
+    }
+    try {
+        SentenceTransformer model(argv[1]);
+        std::vector<std::string> texts;
+        std::ifstream in(argv[2]);
+        for (std::string line; std::getline(in, line);) texts.push_back(line);
+        const std::string pre = argv[3];
+        std::ofstream ids(pre + ".ids", std::ios::binary), batch(pre + ".batch", std::ios::binary),
+            single(pre + ".single", std::ios::binary);
+        for (const auto &t : texts) {
+            const std::vector<int32_t> v = model.tokenize(t);
+            const int32_t n = static_cast<int32_t>(v.size());
+            ids.write(reinterpret_cast<const char *>(&n), 4);
+            ids.write(reinterpret_cast<const char *>(v.data()), 4 * n);
+        }
+        for (const auto &e : model.encode_batch(texts))
+            batch.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());
+        for (const auto &t : texts) {
+            const std::vector<float> e = model.encode(t);
+            single.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());
+        }
+        std::printf("dim %zu, %zu texts\n", model.get_embedding_dimension(), texts.size());
+    } catch (const std::exception &ex) {
+        std::fprintf(stderr, "error: %s\n", ex.what());
+        return 1;
+    }
+    return 0;
+}
