@@ -311,10 +311,12 @@ def ours(args):
 
     if rank == 0:
         traffic = None
-        tpath = os.path.join(ROOT, "profiles", "traffic.json")
+        tpath = os.path.join(ROOT, "profiles", "linear_tcgen05_pair_bge-large.md")
         if os.path.exists(tpath):
             with open(tpath) as f:
-                traffic = json.load(f).get("linear_tcgen05_bytes_per_launch")
+                for ln in f:
+                    if ln.startswith("traffic_bytes_per_launch:"):
+                        traffic = int(ln.split(":")[1])
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -330,6 +332,8 @@ def ours(args):
                          "achieved": gemm_tflops, "peak": sustained_tf, "unit": "TFLOP/s",
                          "frac": gemm_tflops / sustained_tf, "peak_kind": f"bf16 sustained, {peak_kind}",
                          "traffic": traffic,
+                         "traffic_note": "DRAM bytes per launch, mean of the four projection GEMMs of one layer "
+                                         "(ncu, profiles/linear_tcgen05_pair_bge-large.md)",
                          "gemm_flops_per_step": gemm_flops, "gemm_ms_per_step": gemm_ms / args.steps,
                          "attention": {"bound": "hbm", "achieved": attn_gbs, "peak": hbm_gbs, "unit": "GB/s",
                                        "frac": attn_gbs / hbm_gbs, "tflops": attn_tflops,
