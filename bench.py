@@ -258,7 +258,7 @@ def ours(args):
     e1.synchronize()
     barrier()
     elapsed_ms = max_over_ranks(e0.elapsed_time(e1))
-    launches = eng.stats()["launches"] * args.steps
+    launches = sum_over_ranks(float(eng.stats()["launches"] * args.steps))
 
     sentences = sum_over_ranks(float(lengths.size))
     tokens = sum_over_ranks(float(tokens_local))
