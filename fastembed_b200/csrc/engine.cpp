@@ -98,6 +98,7 @@ struct fe_engine {
 
     // activations, sized for the largest batch seen
     DevBuf h32, h16, qkv, attn, y32, ff;
+    DevBuf ln_ws;  // row-statistics exchange of the fused linear + LayerNorm (zero-filled when allocated)
     int64_t cap_tokens = 0;
     // per-call inputs for the host path
     DevBuf d_ids, d_cu, d_out;
@@ -177,6 +178,9 @@ fe_status ensure_activations(fe_engine *e, int64_t T)
     FE_TRY_CUDA(e->attn.ensure(cap * D * 2));
     FE_TRY_CUDA(e->y32.ensure(cap * D * 4));
     FE_TRY_CUDA(e->ff.ensure(cap * F * 2));
+    const size_t ws = fe::linear_layernorm_stats_bytes(cap, static_cast<int64_t>(D));
+    FE_TRY_CUDA(e->ln_ws.ensure(ws));
+    FE_TRY_CUDA(cudaMemset(e->ln_ws.p, 0, ws));
     e->cap_tokens = cap;
     return FE_OK;
 }
@@ -227,6 +231,19 @@ fe_status linear(fe_engine *e, cudaStream_t s, const void *x, const DevBuf &w, c
     return fe::check_cuda(err, "linear");
 }
 
+// h32 <- LayerNorm((x W^T + b) + h32) * g + beta (and its bf16 copy): one fused launch
+// where the shape allows it, else the linear and the LayerNorm separately (y32 scratch).
+fe_status linear_ln(fe_engine *e, cudaStream_t s, const void *x, const DevBuf &w, const DevBuf &b, const DevBuf &g,
+                    const DevBuf &beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k)
+{
+    Scope sc(e, CAT_GEMM, s);
+    fe_status st = FE_OK;
+    cudaError_t err = fe::launch_linear_layernorm(x, w.p, b.as<float>(), g.as<float>(), beta.as<float>(), h32, h16, m,
+                                                  n, k, e->cfg.layer_norm_eps, e->ln_ws.p, e->y32.as<float>(), s, &st);
+    if (st != FE_OK) return st;
+    return fe::check_cuda(err, "linear+LayerNorm");
+}
+
 fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int32_t *cu_host, int batch,
                   float *out, cudaStream_t s)
 {
@@ -259,7 +276,7 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
         if (batch > 0) FE_TRY_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * batch * D, s));
         return FE_OK;
     }
-    float *h32 = e->h32.as<float>(), *y32 = e->y32.as<float>();
+    float *h32 = e->h32.as<float>();
     void *h16 = e->h16.p, *qkv = e->qkv.p, *attn = e->attn.p, *ff = e->ff.p;
     {
         Scope sc(e, CAT_OTHER, s);
@@ -281,20 +298,10 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
             if (st != FE_OK) return st;
             FE_TRY_CUDA(err);
         }
-        // out-proj + bias; the residual add is fused into the LayerNorm that follows
-        FE_TRY(linear(e, s, attn, L.wo, L.bo, nullptr, y32, T, D, D, FE_EPI_BIAS, FE_DTYPE_F32));
-        {
-            Scope sc(e, CAT_OTHER, s);
-            FE_TRY_CUDA(fe::launch_layernorm_dual(y32, h32, L.ln1_g.as<float>(), L.ln1_b.as<float>(), h32, h16, T,
-                                                  static_cast<int>(D), c.layer_norm_eps, s));
-        }
+        // out-proj + bias + residual + LayerNorm, in place on the fp32 residual stream
+        FE_TRY(linear_ln(e, s, attn, L.wo, L.bo, L.ln1_g, L.ln1_b, h32, h16, T, D, D));
         FE_TRY(linear(e, s, h16, L.w1, L.b1, nullptr, ff, T, F, D, act, FE_DTYPE_BF16));
-        FE_TRY(linear(e, s, ff, L.w2, L.b2, nullptr, y32, T, D, F, FE_EPI_BIAS, FE_DTYPE_F32));
-        {
-            Scope sc(e, CAT_OTHER, s);
-            FE_TRY_CUDA(fe::launch_layernorm_dual(y32, h32, L.ln2_g.as<float>(), L.ln2_b.as<float>(), h32,
-                                                  last ? nullptr : h16, T, static_cast<int>(D), c.layer_norm_eps, s));
-        }
+        FE_TRY(linear_ln(e, s, ff, L.w2, L.b2, L.ln2_g, L.ln2_b, h32, last ? nullptr : h16, T, D, F));
     }
     {
         Scope sc(e, CAT_OTHER, s);

@@ -40,11 +40,12 @@ int *current_device_status_word();
 int current_sm_count();
 
 // TMA descriptor for a row-major 2-D tensor [rows, cols] of `elem_bytes` elements
-// with row stride `ld` elements, box [box_rows, box_cols], 128B swizzle unless
-// swizzle128 is false.
+// with row stride `ld` elements, box [box_rows, box_cols], swizzled as `swizzle`
+// (the box row must then be exactly the swizzle width in bytes).
 fe_status make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype,
                        int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld,
-                       uint32_t box_rows, uint32_t box_cols, bool swizzle128 = true);
+                       uint32_t box_rows, uint32_t box_cols,
+                       CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // TMA descriptor for a head-major tensor [heads, rows, 64] of bf16 (each head's
 // rows contiguous), box [1, box_rows, 64], 128B swizzle.
@@ -55,6 +56,15 @@ fe_status make_tmap_heads(CUtensorMap *map, const void *base, uint64_t heads, ui
 cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
                                const float *residual, void *y, int64_t m, int64_t n, int64_t k,
                                int epilogue, int y_dtype, cudaStream_t s, fe_status *st);
+// h32 <- LayerNorm((x W^T + bias) + h32) * gamma + beta; h16 <- bf16 of it (h16 may be
+// null).  stats / y_fallback come from linear_layernorm_split_workspace; the stats
+// region must be zero-filled before its first launch.
+size_t linear_layernorm_workspace_bytes(int64_t m, int64_t n);
+size_t linear_layernorm_stats_bytes(int64_t m, int64_t n);  // the statistics head of it
+void linear_layernorm_split_workspace(void *ws, int64_t m, int64_t n, void **stats, float **y);
+cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *bias, const float *gamma,
+                                    const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
+                                    float eps, void *stats, float *y_fallback, cudaStream_t s, fe_status *st);
 // qkv / out layouts: token-major [T, 3*H*64] / [T, H*64], or head-major
 // [3*H, T, 64] / [H, T, 64] when head_major is true.
 cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, int batch,

@@ -20,7 +20,10 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <mutex>
+#include <unordered_map>
 
 #include "fe_common.cuh"
 #include "fe_internal.h"
@@ -330,6 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // leader (cluster rank 0) issues the MMAs; both CTAs' TMA loads complete on the
 // leader's stage barrier; commits are multicast to the barriers of both CTAs; each
 // CTA's epilogue drains its own 128 accumulator rows and reports back to the leader.
+// Pair p owns tiles p, p + npairs, ...; tile t covers rows (t / n_tiles) * 256 and
+// columns (t % n_tiles) * 256.
 constexpr int P_STAGES = 6;
 constexpr int P_BN = 256;
 constexpr uint32_t P_HALF_BYTES = 128 * BK * 2;        // 16 KB: 128 rows x 64 bf16
@@ -338,6 +343,101 @@ constexpr uint32_t P_TMEM_COLS = 2 * P_BN;
 constexpr uint32_t P_RING_BYTES = P_STAGES * P_STAGE_BYTES;
 constexpr uint32_t P_EPI_BYTES = kEpiWarps * 2 * kStageBufBytes;
 constexpr uint32_t P_SMEM_BYTES = 1024 + P_RING_BYTES + P_EPI_BYTES + 256;
+
+// TMA producer of a pair (lane 0 of warp 0 in both CTAs).
+template <int STAGES>
+__device__ __forceinline__ void pair_producer(uint8_t *ring, uint64_t *full, uint64_t *empty, const CUtensorMap *tm_x,
+                                              const CUtensorMap *tm_w, uint32_t rank, int pair, int npairs,
+                                              int num_tiles, int n_tiles, int k_iters, volatile int *abort_flag,
+                                              int *status)
+{
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed = 0, armed_parity = 0;  // per stage: armed at least once / parity of the last arm
+    for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
+        const int m0 = (tile / n_tiles) * 256;
+        const int n0 = (tile % n_tiles) * P_BN;
+        for (int kb = 0; kb < k_iters; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1)) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            uint8_t *a_dst = ring + stage * P_STAGE_BYTES;
+            uint8_t *b_dst = a_dst + P_HALF_BYTES;
+            const uint32_t leader_full = map_to_rank(&full[stage], 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+            tma_load_2d_pair(a_dst, tm_x, leader_full, kb * BK, m0 + static_cast<int>(rank) * 128);
+            tma_load_2d_pair(b_dst, tm_w, leader_full, kb * BK, n0 + static_cast<int>(rank) * 128);
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1;
+            }
+        }
+    }
+    // The leader's stage barriers count both CTAs' bytes: it drains the pair's loads.
+    if (rank == 0)
+        for (int s = 0; s < STAGES; ++s)
+            if (armed & (1u << s))
+                if (!mbar_wait(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
+}
+
+// MMA issuer of a pair (lane 0 of warp 1 in the leader): 256 x 256 x 64 per stage
+// into one of two TMEM accumulators.
+template <int STAGES>
+__device__ __forceinline__ void pair_mma(uint8_t *ring, uint64_t *full, uint64_t *empty, uint64_t *acc_full,
+                                         uint64_t *acc_empty, uint32_t tmem_base, int pair, int npairs, int num_tiles,
+                                         int k_iters, volatile int *abort_flag, int *status)
+{
+    constexpr uint32_t idesc = idesc_bf16_f32(256, P_BN, false, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool issued = false;
+    for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) {
+            report(status, DEV_TIMEOUT);
+            *abort_flag = 1;
+            break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * P_BN;
+        for (int kb = 0; kb < k_iters; ++kb) {
+            if (!mbar_wait(&full[stage], phase)) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(ring + stage * P_STAGE_BYTES);
+            const uint64_t ad = sdesc_sw128(a_addr, 16, 1024);
+            const uint64_t bd = sdesc_sw128(a_addr + P_HALF_BYTES, 16, 1024);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K step inside the swizzle atom
+                umma_f16_ss_pair(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * 2), idesc,
+                                 (kb | k) != 0 ? 1u : 0u);
+            issued = true;
+            umma_commit_pair_both(&empty[stage]);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1;
+            }
+        }
+        if (*abort_flag) break;
+        umma_commit_pair_both(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+    }
+    if (*abort_flag && issued) {
+        // Let outstanding MMAs retire before TMEM is released.
+        uint64_t *probe = &acc_full[acc];
+        umma_commit_pair_both(probe);
+        if (!mbar_wait(probe, acc_phase)) report(status, DEV_TIMEOUT);
+    }
+}
 
 template <bool OUT_BF16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -392,89 +492,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        if (lane == 0) {
-            // ---------------- TMA producer (both CTAs)
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t armed = 0, armed_parity = 0;
-            for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
-                const int m0 = (tile / n_tiles) * 256;
-                const int n0 = (tile % n_tiles) * P_BN;
-                for (int kb = 0; kb < k_iters; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1)) {
-                        report(status, DEV_TIMEOUT);
-                        *abort_flag = 1;
-                        break;
-                    }
-                    uint8_t *a_dst = ring + stage * P_STAGE_BYTES;
-                    uint8_t *b_dst = a_dst + P_HALF_BYTES;
-                    const uint32_t leader_full = map_to_rank(&full[stage], 0);
-                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
-                    tma_load_2d_pair(a_dst, &tm_x, leader_full, kb * BK, m0 + static_cast<int>(rank) * 128);
-                    tma_load_2d_pair(b_dst, &tm_w, leader_full, kb * BK, n0 + static_cast<int>(rank) * 128);
-                    armed |= 1u << stage;
-                    armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-                    if (++stage == P_STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
-                }
-            }
-            // The leader's stage barriers count both CTAs' bytes: it drains the pair's loads.
-            if (rank == 0)
-                for (int s = 0; s < P_STAGES; ++s)
-                    if (armed & (1u << s))
-                        if (!mbar_wait(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
-        }
+        if (lane == 0)
+            pair_producer<P_STAGES>(ring, full, empty, &tm_x, &tm_w, rank, pair, npairs, num_tiles, n_tiles, k_iters,
+                                    abort_flag, status);
     } else if (warp == 1) {
-        if (lane == 0 && rank == 0) {
-            // ---------------- MMA issuer (leader only)
-            constexpr uint32_t idesc = idesc_bf16_f32(256, P_BN, false, false);
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool issued = false;
-            for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
-                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) {
-                    report(status, DEV_TIMEOUT);
-                    *abort_flag = 1;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * P_BN;
-                for (int kb = 0; kb < k_iters; ++kb) {
-                    if (!mbar_wait(&full[stage], phase)) {
-                        report(status, DEV_TIMEOUT);
-                        *abort_flag = 1;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_u32(ring + stage * P_STAGE_BYTES);
-                    const uint64_t ad = sdesc_sw128(a_addr, 16, 1024);
-                    const uint64_t bd = sdesc_sw128(a_addr + P_HALF_BYTES, 16, 1024);
-#pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K step inside the swizzle atom
-                        umma_f16_ss_pair(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * 2),
-                                         idesc, (kb | k) != 0 ? 1u : 0u);
-                    issued = true;
-                    umma_commit_pair_both(&empty[stage]);
-                    if (++stage == P_STAGES) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
-                }
-                if (*abort_flag) break;
-                umma_commit_pair_both(&acc_full[acc]);
-                acc ^= 1;
-                if (acc == 0) acc_phase ^= 1;
-            }
-            if (*abort_flag && issued) {
-                uint64_t *probe = &acc_full[acc];
-                umma_commit_pair_both(probe);
-                if (!mbar_wait(probe, acc_phase)) report(status, DEV_TIMEOUT);
-            }
-        }
+        if (lane == 0 && rank == 0)
+            pair_mma<P_STAGES>(ring, full, empty, acc_full, acc_empty, tmem_base, pair, npairs, num_tiles, k_iters,
+                               abort_flag, status);
     } else {
         // ---------------- epilogue (warps 2..5 of both CTAs)
         const int q = warp & 3;
@@ -516,6 +540,414 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Linear + residual + LayerNorm in one kernel:
+//     h32 <- LayerNorm((x W^T + bias) + h32) * gamma + beta,   h16 <- bf16(h32)
+// the out-projection / FFN-down step of a post-LN encoder layer (reference:
+// src/sentence_transformers_impl.cpp:250-263 and :403-436, LayerNorm statistics as in
+// src/ops/cpu/cpu_matrix_ops.cpp:64-92).  The mainloop is the pair kernel's.  A row of
+// N = 256 * n_tiles columns spans n_tiles tiles, which run on different pairs at the
+// same time, so LayerNorm statistics are exchanged through global memory:
+//   pass 1   each epilogue warp forms x = (acc + bias) + residual for its 32 rows (the
+//            residual arrives by TMA), writes x back into its TMEM accumulator and
+//            computes each row's (mean, M2) over its columns: exact two-pass per
+//            32-column chunk, chunks (all the same size) combined exactly;
+//   exchange each row's partial goes to stats[row][part] as two 64-bit words holding the
+//            value and the launch's epoch, so a reader that sees the epoch sees the value
+//            (single-copy atomic 64-bit accesses): no counter, no fence.  The warp polls
+//            its rows' other parts (bounded wait) and combines them in part order, so the
+//            result does not depend on arrival order;
+//   pass 2   x is read back from TMEM, normalised and TMA-stored as fp32 (in place over the
+//            residual) and bf16.
+// The waiting needs every pair of the launch resident at once and every row group's
+// tiles in the same round: the launcher sizes the grid from the occupancy of this
+// kernel, as a multiple of n_tiles, and orders launches of this kernel on a device one
+// after another.
+//
+// Configurations: ring stages, epilogue warps (4 or 8; 8 = two per TMEM lane quarter,
+// splitting the 256 columns) and 4 KB fp32 slabs per epilogue warp (plus one 2 KB bf16
+// slab); shared memory is the binding limit.  The launcher uses this kernel for
+// K >= 2048 only.  Every tile's accumulator stays in TMEM from the end of its mainloop
+// until its row statistics have crossed between pairs (a few microseconds of L2 round
+// trips), and with two accumulators the next-but-one mainloop waits for that.  A K = 4096
+// mainloop (~25 us a tile) hides it; a K = 1024 one (~7 us) does not: measured on the
+// bge-large out-projection, 102-138 us fused against 51 + 59 us for the pair kernel and
+// the LayerNorm kernel, which the launcher uses there instead.
+constexpr uint32_t L_BAR_BYTES = 512;
+template <int STAGES, int EPI_WARPS, int SLABS>
+struct LnCfg {
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int COLS = P_BN / (EPI_WARPS / 4);  // accumulator columns per epilogue warp
+    static constexpr int CH = COLS / 32;                 // 32-column chunks per warp
+    static constexpr uint32_t WARP_BYTES = SLABS * 4096 + 2048;
+    static constexpr uint32_t RING = STAGES * P_STAGE_BYTES;
+    static constexpr uint32_t EPI = EPI_WARPS * WARP_BYTES;
+    static constexpr uint32_t VEC = 3 * P_BN * 4;  // bias, gamma, beta of the pair's 256 columns
+    static constexpr uint32_t SMEM = 1024 + RING + EPI + VEC + L_BAR_BYTES;
+    static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "epilogue warps");
+    static_assert(SLABS == 1 || SLABS == 2, "fp32 slabs");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+using LnLongK = LnCfg<6, 4, 1>;
+
+struct LnParams {
+    const float *bias;
+    const float *gamma;
+    const float *beta;
+    unsigned long long *stats;  // [M][nparts][2]: (mean, M2) of each row over each warp's columns,
+                                // each word = float bits << 32 | epoch
+    unsigned epoch;             // nonzero, unique per launch on this workspace
+    float eps;
+    int nparts;                 // statistics partials per row = N / COLS
+};
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long tag(float v, unsigned epoch)
+{
+    return (static_cast<unsigned long long>(__float_as_uint(v)) << 32) | epoch;
+}
+
+template <int STAGES, int EPI_WARPS, int SLABS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WARPS, SLABS>::THREADS, 1)
+    linear_ln_tcgen05_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                           const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_h16,
+                           int M, int N, int K, LnParams p, int write16, int *status)
+{
+    using C = LnCfg<STAGES, EPI_WARPS, SLABS>;
+    constexpr int COLS = C::COLS, CH = C::CH;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = smem;
+    uint8_t *epi_buf = smem + C::RING;
+    float *vec = reinterpret_cast<float *>(epi_buf + C::EPI);  // [3][256]
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi_buf + C::EPI + C::VEC);
+    uint64_t *empty = full + STAGES;
+    uint64_t *acc_full = empty + STAGES;  // [2]
+    uint64_t *acc_empty = acc_full + 2;   // [2]
+    uint64_t *res_bar = acc_empty + 2;    // [EPI_WARPS][SLABS]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_bar + SLABS * EPI_WARPS);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    static_assert((2 * STAGES + 4 + SLABS * EPI_WARPS) * 8 + 8 <= L_BAR_BYTES, "barrier space");
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;  // a multiple of n_tiles: every tile of this pair has the same columns
+    const int m_tiles = (M + 255) / 256;
+    const int n_tiles = N / P_BN;
+    const int num_tiles = m_tiles * n_tiles;
+    const int k_iters = (K + BK - 1) / BK;
+    const int n0 = (pair % n_tiles) * P_BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * EPI_WARPS);
+        }
+        for (int b = 0; b < SLABS * EPI_WARPS; ++b) mbar_init(&res_bar[b], 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_h);
+        if (write16) tma_prefetch_desc(&tm_h16);
+    }
+    for (int i = threadIdx.x; i < 3 * P_BN; i += blockDim.x) {
+        const float *src = i < P_BN ? p.bias : (i < 2 * P_BN ? p.gamma : p.beta);
+        vec[i] = src[n0 + (i % P_BN)];
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, P_TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0)
+            pair_producer<STAGES>(ring, full, empty, &tm_x, &tm_w, rank, pair, npairs, num_tiles, n_tiles, k_iters,
+                                  abort_flag, status);
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0)
+            pair_mma<STAGES>(ring, full, empty, acc_full, acc_empty, tmem_base, pair, npairs, num_tiles, k_iters,
+                             abort_flag, status);
+    } else {
+        // ---------------- epilogue: warp w drains TMEM lanes 32 * (w % 4) (the lane-quarter
+        // rule), accumulator columns [h * COLS, (h + 1) * COLS), h = (w - 2) / 4.
+        // Staging per warp: SLABS 4 KB fp32 slabs (residual in pass 1, output in pass 2)
+        // and one 2 KB bf16 output slab.
+        const int ew = warp - 2;
+        const int q = warp & 3;
+        const int h = ew >> 2;
+        const int c0 = n0 + h * COLS;  // first column of this warp
+        uint8_t *wb = epi_buf + ew * C::WARP_BYTES;
+        uint8_t *hs = wb + SLABS * 4096;
+        uint64_t *rbar = res_bar + SLABS * ew;
+        const float *vb = vec + h * COLS, *vg = vec + P_BN + h * COLS, *ve = vec + 2 * P_BN + h * COLS;
+        const int part = c0 / COLS;
+        const uint32_t leader_acc_empty[2] = {map_to_rank(&acc_empty[0], 0), map_to_rank(&acc_empty[1], 0)};
+        uint32_t rpar = 0;      // bit b: parity of the next completion of rbar[b]
+        uint32_t inflight = 0;  // bit b: a residual load into slab b has not been waited for
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        const float inv_n = 1.0f / static_cast<float>(N);
+        auto warp_row0 = [&](int t) { return (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + q * 32; };
+        auto load_res = [&](int b, int col, int row) {  // lane 0
+            mbar_arrive_expect_tx(&rbar[b], 4096);
+            tma_load_2d(wb + b * 4096, &tm_h, &rbar[b], col, row);
+        };
+        if (lane < CH && pair < num_tiles) tma_prefetch_l2_2d(&tm_h, c0 + 32 * lane, warp_row0(pair));
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
+            if (*abort_flag) break;
+            const int row0 = warp_row0(tile);
+            const int row = row0 + lane;
+            if (lane < CH && tile + npairs < num_tiles)
+                tma_prefetch_l2_2d(&tm_h, c0 + 32 * lane, warp_row0(tile + npairs));
+            if (lane == 0) {
+                bulk_wait_read<0>();  // the previous tile's stores have read every slab
+                load_res(0, c0, row0);
+            }
+            inflight = 1;
+            __syncwarp();
+            if (!mbar_wait(&acc_full[acc], acc_phase)) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN + h * COLS;
+
+            // ---- pass 1: x = (acc + bias) + residual back into TMEM; per-chunk mean / M2
+            float cm[CH], cq_sum = 0.f;
+            bool ok = true;
+            uint32_t v[2][32];
+            tmem_ld_x32(t_row, v[0]);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int b = c % SLABS;
+                uint32_t(&cur)[32] = v[c & 1];
+                tmem_wait_ld_regs(cur);
+                if (c + 1 < CH) {
+                    if (c >= 1) tmem_wait_st();  // v[(c + 1) & 1] was the source of the previous store
+                    tmem_ld_x32(t_row + (c + 1) * 32, v[(c + 1) & 1]);
+                    if (SLABS == 2) {  // the other slab was consumed by chunk c - 1
+                        if (lane == 0) load_res((c + 1) % SLABS, c0 + 32 * (c + 1), row0);
+                        inflight |= 1u << ((c + 1) % SLABS);
+                    }
+                }
+                if (!mbar_wait(&rbar[b], (rpar >> b) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                rpar ^= 1u << b;
+                inflight &= ~(1u << b);
+                const uint8_t *rs = wb + b * 4096 + lane * 128;
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 r = *reinterpret_cast<const uint4 *>(rs + ((j ^ (lane & 7)) << 4));
+                    const float4 bb = *reinterpret_cast<const float4 *>(vb + c * 32 + 4 * j);
+                    const float x0 = (__uint_as_float(cur[4 * j + 0]) + bb.x) + __uint_as_float(r.x);
+                    const float x1 = (__uint_as_float(cur[4 * j + 1]) + bb.y) + __uint_as_float(r.y);
+                    const float x2 = (__uint_as_float(cur[4 * j + 2]) + bb.z) + __uint_as_float(r.z);
+                    const float x3 = (__uint_as_float(cur[4 * j + 3]) + bb.w) + __uint_as_float(r.w);
+                    cur[4 * j + 0] = __float_as_uint(x0);
+                    cur[4 * j + 1] = __float_as_uint(x1);
+                    cur[4 * j + 2] = __float_as_uint(x2);
+                    cur[4 * j + 3] = __float_as_uint(x3);
+                    s4[0] += x0;
+                    s4[1] += x1;
+                    s4[2] += x2;
+                    s4[3] += x3;
+                }
+                __syncwarp();  // every lane has read slab b
+                if (SLABS == 1 && c + 1 < CH) {
+                    if (lane == 0) load_res(0, c0 + 32 * (c + 1), row0);
+                    inflight |= 1u;
+                }
+                cm[c] = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 32.0f);
+                float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float d = __uint_as_float(cur[j]) - cm[c];
+                    q4[j & 3] += d * d;
+                }
+                cq_sum += (q4[0] + q4[1]) + (q4[2] + q4[3]);
+                tmem_st_x32(t_row + c * 32, cur);
+            }
+            tmem_wait_ld();
+            tmem_wait_st();
+            if (!ok) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            // this warp's (mean, M2) over its COLS columns: equal-size chunks combined exactly
+            float mean = 0.f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) mean += cm[c];
+            mean *= 1.0f / CH;
+            float m2 = 0.f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const float d = cm[c] - mean;
+                m2 += d * d;
+            }
+            m2 = cq_sum + 32.0f * m2;
+
+            // ---- publish, then collect the row's other parts (data and epoch in one
+            // 64-bit word each: no fences, no counters)
+            unsigned long long *sp = p.stats + (static_cast<size_t>(row) * p.nparts) * 2;
+            if (row < M) {
+                st_relaxed_u64(sp + 2 * part, tag(mean, p.epoch));
+                st_relaxed_u64(sp + 2 * part + 1, tag(m2, p.epoch));
+            }
+            // The parts' means are accumulated about the first one (shifted sums), so that
+            // no per-part value has to stay live: gm = K + S1 / P,
+            // M2 = sum(M2_i) + COLS * (S2 - S1^2 / P).
+            constexpr int kMaxParts = 2048 / COLS;  // rows of up to 2048 columns
+            float pk = 0.f, ps1 = 0.f, ps2 = 0.f, pq_sum = 0.f;
+            bool ready = row >= M;
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t it = 0;; ++it) {
+                if (!ready) {
+                    const unsigned long long a0 = ld_relaxed_u64(sp);
+                    bool all = static_cast<unsigned>(a0) == p.epoch;
+                    const float k0 = __uint_as_float(static_cast<unsigned>(a0 >> 32));
+                    float s1 = 0.f, s2 = 0.f, qs = 0.f;
+#pragma unroll
+                    for (int i = 0; i < kMaxParts; ++i)
+                        if (i < p.nparts) {
+                            const unsigned long long a = i == 0 ? a0 : ld_relaxed_u64(sp + 2 * i);
+                            const unsigned long long bq = ld_relaxed_u64(sp + 2 * i + 1);
+                            all = all && static_cast<unsigned>(a) == p.epoch && static_cast<unsigned>(bq) == p.epoch;
+                            const float d = __uint_as_float(static_cast<unsigned>(a >> 32)) - k0;
+                            s1 += d;
+                            s2 += d * d;
+                            qs += __uint_as_float(static_cast<unsigned>(bq >> 32));
+                        }
+                    ready = all;
+                    pk = k0;
+                    ps1 = s1;
+                    ps2 = s2;
+                    pq_sum = qs;
+                }
+                if (__all_sync(0xffffffffu, ready)) break;
+                const bool stop = (it & 15u) == 15u && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs);
+                if (__any_sync(0xffffffffu, stop)) {  // the same decision in every lane
+                    ok = false;
+                    break;
+                }
+            }
+            if (!ok) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            float gm = 0.f, gq = 0.f;
+            if (row < M) {
+                const float inv_p = 1.0f / static_cast<float>(p.nparts);
+                gm = pk + ps1 * inv_p;
+                gq = pq_sum + static_cast<float>(COLS) * fmaxf(ps2 - ps1 * ps1 * inv_p, 0.f);
+            }
+            const float inv_sd = 1.0f / sqrtf(gq * inv_n + p.eps);
+
+            // ---- pass 2: normalise from TMEM, TMA-store fp32 and bf16.  Bulk groups per
+            // chunk c: F(c) (fp32 slab c % SLABS), then B(c) (the bf16 slab).
+            tmem_ld_x32(t_row, v[0]);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int b = c % SLABS;
+                uint32_t(&cur)[32] = v[c & 1];
+                tmem_wait_ld_regs(cur);
+                if (c + 1 < CH) tmem_ld_x32(t_row + (c + 1) * 32, v[(c + 1) & 1]);
+                float o[32];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 g = *reinterpret_cast<const float4 *>(vg + c * 32 + 4 * j);
+                    const float4 e = *reinterpret_cast<const float4 *>(ve + c * 32 + 4 * j);
+                    o[4 * j + 0] = (__uint_as_float(cur[4 * j + 0]) - gm) * inv_sd * g.x + e.x;
+                    o[4 * j + 1] = (__uint_as_float(cur[4 * j + 1]) - gm) * inv_sd * g.y + e.y;
+                    o[4 * j + 2] = (__uint_as_float(cur[4 * j + 2]) - gm) * inv_sd * g.z + e.z;
+                    o[4 * j + 3] = (__uint_as_float(cur[4 * j + 3]) - gm) * inv_sd * g.w + e.w;
+                }
+                // F(c - SLABS) has read slab b: at most 2 * SLABS - 1 newer groups pending
+                if (lane == 0) bulk_wait_read<2 * SLABS - 1>();
+                __syncwarp();
+                uint8_t *fs = wb + b * 4096;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<uint4 *>(fs + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_uint4(__float_as_uint(o[4 * j + 0]), __float_as_uint(o[4 * j + 1]),
+                                   __float_as_uint(o[4 * j + 2]), __float_as_uint(o[4 * j + 3]));  // 128B swizzle
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tm_h, fs, c0 + c * 32, row0);
+                    bulk_commit();
+                }
+                if (write16) {
+                    if (lane == 0) bulk_wait_read<1>();  // B(c - 1) has read the bf16 slab
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        *reinterpret_cast<uint4 *>(hs + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                            make_uint4(pack_bf16x2(o[8 * j + 0], o[8 * j + 1]), pack_bf16x2(o[8 * j + 2], o[8 * j + 3]),
+                                       pack_bf16x2(o[8 * j + 4], o[8 * j + 5]),
+                                       pack_bf16x2(o[8 * j + 6], o[8 * j + 7]));  // 64B swizzle
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                }
+                if (lane == 0) {  // an empty group keeps the F / B alternation when bf16 is not written
+                    if (write16) tma_store_2d(&tm_h16, hs, c0 + c * 32, row0);
+                    bulk_commit();
+                }
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(leader_acc_empty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+        // Residual loads still in flight (abandoned tiles) must land before the CTA exits.
+        if (lane == 0) {
+            for (int b = 0; b < SLABS; ++b)
+                if (inflight & (1u << b))
+                    if (!mbar_wait(&rbar[b], (rpar >> b) & 1u)) report(status, DEV_TIMEOUT);
+            bulk_wait_all<0>();
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, P_TMEM_COLS);
+    }
+}
+
 template <bool OUT_BF16>
 cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N, int K,
                         const float *bias, const float *residual, int epi, int *status, cudaStream_t s)
@@ -536,6 +968,30 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
     linear_tcgen05_pair<OUT_BF16><<<2 * pairs, kThreads, P_SMEM_BYTES, s>>>(tx, tw, ty, M, N, K, bias, residual, epi,
                                                                            status);
     return cudaGetLastError();
+}
+
+// Pairs of linear_ln_tcgen05_pair<Cfg> that can be resident at once on the current
+// device (0 if unknown).
+template <class Cfg, int STAGES, int EPI_WARPS, int SLABS>
+int ln_resident_pairs()
+{
+    static int cached[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && cached[dev] > 0) return cached[dev];
+    auto kern = linear_ln_tcgen05_pair<STAGES, EPI_WARPS, SLABS>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (dev < 64) cached[dev] = clusters;
+    return clusters;
 }
 
 template <int BN, bool OUT_BF16>
@@ -609,6 +1065,120 @@ cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
                         : launch<256, false>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s);
     return out_bf16 ? launch<128, true>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s)
                     : launch<128, false>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s);
+}
+
+}  // namespace fe
+
+namespace fe {
+namespace {
+
+constexpr int kMaxLnParts = 8;  // rows of up to 2048 columns
+
+size_t round_up_256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Launches of linear_ln_tcgen05_pair on one device run one after another, whatever
+// their streams: a launch waits for the previous one's completion event.  Two such
+// launches running at once could each hold SMs that the other's waiting pairs need.
+std::mutex g_ln_mu;
+cudaEvent_t g_ln_last[64] = {};
+// Next epoch of each statistics workspace (keyed by its address); 0 is never used, so
+// a zero-filled workspace holds no valid partial.
+std::unordered_map<const void *, unsigned> g_ln_epoch;
+
+}  // namespace
+
+// Workspace layout: [stats: two 64-bit words per row and 128-column part]
+// [fp32 [m, n] scratch of the unfused form].
+size_t linear_layernorm_stats_bytes(int64_t m, int64_t n)
+{
+    return round_up_256(static_cast<size_t>(m) * static_cast<size_t>((n + 127) / 128) * 16);
+}
+
+size_t linear_layernorm_workspace_bytes(int64_t m, int64_t n)
+{
+    return linear_layernorm_stats_bytes(m, n) + static_cast<size_t>(m) * static_cast<size_t>(n) * 4;
+}
+
+void linear_layernorm_split_workspace(void *ws, int64_t m, int64_t n, void **stats, float **y)
+{
+    *stats = ws;
+    *y = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + linear_layernorm_stats_bytes(m, n));
+}
+
+cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *bias, const float *gamma,
+                                    const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
+                                    float eps, void *stats, float *y_fallback, cudaStream_t s, fe_status *st)
+{
+    *st = FE_OK;
+    if (m == 0 || n == 0) return cudaSuccess;
+    const int n_tiles = static_cast<int>(n / P_BN);
+    // fused only where the mainloop hides the statistics exchange (see linear_ln_tcgen05_pair)
+    bool fused = k >= 2048 && pair_mode_enabled() && n % P_BN == 0 && n_tiles <= kMaxLnParts && stats;
+    int pairs = 0;
+    if (fused) {
+        const int tiles = static_cast<int>((m + 255) / 256) * n_tiles;
+        pairs = std::min(ln_resident_pairs<LnLongK, 6, 4, 1>(), current_sm_count() / 2);
+        pairs = pairs / n_tiles * n_tiles;  // each row group's tiles in the same round
+        if (pairs > tiles) pairs = tiles;
+        fused = pairs >= n_tiles;
+    }
+    if (!fused) {
+        // Unfused form of the same step: linear with bias into fp32, then residual + LayerNorm.
+        if (!y_fallback) {
+            *st = fail(FE_ERR_INVALID_ARGUMENT, "linear+LayerNorm: no fp32 scratch for this shape");
+            return cudaSuccess;
+        }
+        cudaError_t e = launch_linear_bf16(x, w, bias, nullptr, y_fallback, m, n, k, FE_EPI_BIAS, FE_DTYPE_F32, s, st);
+        if (e != cudaSuccess || *st != FE_OK) return e;
+        return launch_layernorm_dual(y_fallback, h32, gamma, beta, h32, h16, m, static_cast<int>(n), eps, s);
+    }
+    CUtensorMap tx, tw, th, th16;
+    fe_status r = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, k, k, BM, BK);
+    if (r == FE_OK) r = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, k, k, 128, BK);
+    if (r == FE_OK) r = make_tmap_2d(&th, h32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, n, n, 32, 32);
+    if (r == FE_OK)
+        r = h16 ? make_tmap_2d(&th16, h16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, n, n, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_64B)
+                : make_tmap_2d(&th16, h32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, n, n, 32, 32);  // not used
+    if (r != FE_OK) {
+        *st = r;
+        return cudaSuccess;
+    }
+    LnParams p;
+    p.bias = bias;
+    p.gamma = gamma;
+    p.beta = beta;
+    p.stats = static_cast<unsigned long long *>(stats);
+    p.eps = eps;
+    p.nparts = static_cast<int>(n / LnLongK::COLS);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cap);
+    const bool order = cap == cudaStreamCaptureStatusNone && dev < 64;
+    std::lock_guard<std::mutex> lock(g_ln_mu);
+    unsigned &ep = g_ln_epoch[stats];
+    if (++ep == 0) ep = 1;
+    p.epoch = ep;
+    if (order && g_ln_last[dev]) {
+        cudaError_t e = cudaStreamWaitEvent(s, g_ln_last[dev], 0);
+        if (e != cudaSuccess) return e;
+    }
+    const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
+    const int w16 = h16 != nullptr;
+    int *status = current_device_status_word();
+    linear_ln_tcgen05_pair<6, 4, 1><<<2 * pairs, LnLongK::THREADS, LnLongK::SMEM, s>>>(tx, tw, th, th16, M, N, K, p,
+                                                                                        w16, status);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (order) {
+        if (!g_ln_last[dev]) {
+            e = cudaEventCreateWithFlags(&g_ln_last[dev], cudaEventDisableTiming);
+            if (e != cudaSuccess) return e;
+        }
+        e = cudaEventRecord(g_ln_last[dev], s);
+    }
+    return e;
 }
 
 }  // namespace fe

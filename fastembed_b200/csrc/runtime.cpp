@@ -97,7 +97,7 @@ fe_status load_encode()
 
 fe_status make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes,
                        uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows, uint32_t box_cols,
-                       bool swizzle128)
+                       CUtensorMapSwizzle swizzle)
 {
     FE_TRY(load_encode());
     if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
@@ -109,9 +109,7 @@ fe_status make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType d
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         char buf[160];
         std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d) for [%llu x %llu] box [%u x %u]",

@@ -127,6 +127,26 @@ def layernorm_dual(x, gamma, beta, eps, residual=None):
     return h32, h16
 
 
+def linear_layernorm_workspace(m, n, device):
+    """A zero-filled workspace for linear_layernorm of [m, n] rows (reusable across calls)."""
+    size = C.c_size_t(0)
+    call("fe_linear_layernorm_workspace_bytes", m, n, C.byref(size))
+    return torch.zeros(max(int(size.value), 1), dtype=torch.uint8, device=device)
+
+
+def linear_layernorm(x, w, bias, gamma, beta, h32, eps, workspace=None, want_h16=True):
+    """h32 <- LayerNorm((x @ w.T + bias) + h32) * gamma + beta in place; returns (h32, h16)."""
+    _cuda(x, w, bias, gamma, beta, h32)
+    m, k = x.shape
+    n = w.shape[0]
+    if workspace is None:
+        workspace = linear_layernorm_workspace(m, n, x.device)
+    h16 = torch.empty(m, n, dtype=torch.bfloat16, device=x.device) if want_h16 else None
+    call("fe_linear_layernorm_bf16", _p(x), _p(w), _p(bias), _p(gamma), _p(beta), _p(h32), _p(h16), m, n, k, eps,
+         _p(workspace), workspace.numel(), _s(x))
+    return h32, h16
+
+
 def pool_l2(h, cu_seqlens, mode="cls"):
     _cuda(h, cu_seqlens)
     B = cu_seqlens.numel() - 1

@@ -163,6 +163,21 @@ fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int3
  * src/sentence_transformers_impl.cpp:255-266 and :429-437.  h32 may alias residual. */
 fe_status fe_layernorm_dual(const float *x, const float *residual, const float *gamma, const float *beta,
                             float *h32, void *h16, int64_t rows, int32_t dim, float eps, fe_stream_t stream);
+/* Projection, residual add and LayerNorm in one launch:
+ *     h32 <- LayerNorm((x[m,k] · w[n,k]^T + bias) + h32) * gamma + beta   (in place)
+ *     h16 <- bf16(h32)                                                  (when h16 != NULL)
+ * The out-projection and FFN-down steps of a post-LN encoder layer, each with the
+ * residual add and LayerNorm that follow it (src/sentence_transformers_impl.cpp:250-266
+ * and :403-437; LayerNorm as in src/ops/cpu/cpu_matrix_ops.cpp:64-92).  Requires
+ * k % 8 == 0 and n in {128, 256, 384, 512, 768, 1024, 1536, 2048}; 16-byte aligned
+ * pointers.  `workspace` holds fe_linear_layernorm_workspace_bytes(m, n) bytes and
+ * must be zero-filled before its first use; it then serves any number of calls, with
+ * any m up to the one it was sized for.  Calls that share a workspace must not run
+ * concurrently. */
+fe_status fe_linear_layernorm_workspace_bytes(int64_t m, int64_t n, size_t *bytes);
+fe_status fe_linear_layernorm_bf16(const void *x, const void *w, const float *bias, const float *gamma,
+                                   const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
+                                   float eps, void *workspace, size_t workspace_bytes, fe_stream_t stream);
 /* Per-sentence pooling + L2 normalisation of packed hidden states h [total, dim]
  * into out [batch, dim].  Replaces src/sentence_transformers_impl.cpp:289-341. */
 fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, int32_t dim,

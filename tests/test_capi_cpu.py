@@ -22,6 +22,7 @@ def declared_functions():
 def test_header_declares_the_op_and_engine_api():
     names = declared_functions()
     for must in ("fe_linear_bf16", "fe_attention_varlen_bf16", "fe_embed_layernorm", "fe_layernorm_dual",
+                 "fe_linear_layernorm_bf16",
                  "fe_pool_l2", "fe_sgemm_nt", "fe_mha_f32", "fe_engine_create", "fe_engine_encode_packed",
                  "fe_engine_encode_host", "fe_plan_shards"):
         assert must in names
@@ -56,6 +57,14 @@ def test_validation_happens_before_any_device_work(fe_lib):
     assert b"divisible" in L.fe_last_error_message()
     assert L.fe_embed_layernorm(buf, buf, 1, 4, buf, buf, buf, buf, buf, 100, 10, 10, 1e-12, buf, buf, None) == 4
     assert L.fe_pool_l2(buf, buf, 1, 64, 9, buf, None) == 1
+    size = C.c_size_t(0)
+    assert L.fe_linear_layernorm_workspace_bytes(4097, 1024, C.byref(size)) == 0
+    assert size.value >= 4097 * 1024 * 4 + 4097 * 4 * 8  # fp32 scratch + (mean, M2) per row and part
+    assert L.fe_linear_layernorm_workspace_bytes(4, 1024, None) == 1
+    assert L.fe_linear_layernorm_bf16(buf, buf, buf, buf, buf, buf, None, 4, 640, 64, 1e-12, buf, 1 << 30,
+                                      None) == 4  # row width 640 unsupported
+    assert L.fe_linear_layernorm_bf16(buf, buf, buf, buf, buf, buf, None, 4, 1024, 64, 1e-12, buf, 64,
+                                      None) == 1  # workspace too small
     # zero-sized work is a no-op
     assert L.fe_linear_bf16(None, None, None, None, None, 0, 8, 64, EPI["none"], DTYPE["bf16"], None) == 0
 

@@ -179,6 +179,82 @@ def test_layernorm_dual(cuda_dev):
             assert torch.equal(h16r, h32r.to(torch.bfloat16))
 
 
+# ----------------------------------------- linear + residual + LayerNorm, one launch
+def _linear_ln_ref(x, w, b, res, gam, bet, eps):
+    y = (x.float() @ w.float().T + b) + res
+    return torch.nn.functional.layer_norm(y, (w.shape[0],), gam, bet, eps)
+
+
+def _linear_ln_inputs(m, n, k, seed, dev):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    b = torch.randn(n, device=dev, generator=g) * 0.1
+    res = torch.randn(m, n, device=dev, generator=g) * 2 + 0.5
+    gam = torch.randn(n, device=dev, generator=g)
+    bet = torch.randn(n, device=dev, generator=g)
+    return x, w, b, res, gam, bet
+
+
+# (m, n, k): the one-launch form (k >= 2048) with the row-statistics exchange across 4, 3,
+# 1, 2 and 8 column tiles of 256, a single 256-row tile among them; and the two-launch
+# form (linear, then LayerNorm) for k < 2048 and for n = 384.
+LINEAR_LN_SHAPES = [(700, 1024, 4096), (4097, 768, 3072), (300, 256, 2048), (33, 512, 2048), (1000, 2048, 2048),
+                    (700, 1024, 1024), (520, 384, 384)]
+
+
+@pytest.mark.parametrize("pair", ["1", "0"])
+@pytest.mark.parametrize("m,n,k", LINEAR_LN_SHAPES)
+def test_linear_layernorm(cuda_dev, monkeypatch, m, n, k, pair):
+    """h32 <- LN((x W^T + b) + h32) against the fp32 composition of the same steps;
+    FE_LINEAR_PAIR=0 takes the two-launch form for every shape."""
+    from fastembed_b200 import ops
+    monkeypatch.setenv("FE_LINEAR_PAIR", pair)
+    x, w, b, res, gam, bet = _linear_ln_inputs(m, n, k, m + n + k, cuda_dev)
+    ref = _linear_ln_ref(x, w, b, res, gam, bet, 1e-12)
+    h32, h16 = ops.linear_layernorm(x, w, b, gam, bet, res.clone(), 1e-12)
+    torch.cuda.synchronize()
+    assert float((h32 - ref).abs().max()) < 1e-4
+    assert torch.equal(h16, h32.to(torch.bfloat16))
+    ops.device_status(0)
+
+
+def test_linear_layernorm_workspace_reuse_and_determinism(cuda_dev):
+    """One workspace sized for the largest m serves calls with smaller m in between
+    (every call leaves its counters at zero); repeated calls are bit-identical, a row
+    block computed alone equals its rows of the batch, and h16 may be omitted."""
+    from fastembed_b200 import ops
+    n, k = 1024, 4096
+    ws = ops.linear_layernorm_workspace(4097, n, cuda_dev)
+    outs = {}
+    for m in (4097, 700, 4097, 137, 700):
+        x, w, b, res, gam, bet = _linear_ln_inputs(m, n, k, m, cuda_dev)
+        h32, h16 = ops.linear_layernorm(x, w, b, gam, bet, res.clone(), 1e-12, workspace=ws)
+        torch.cuda.synchronize()
+        assert float((h32 - _linear_ln_ref(x, w, b, res, gam, bet, 1e-12)).abs().max()) < 1e-4
+        if m in outs:
+            assert torch.equal(outs[m], h32)
+        outs[m] = h32
+    x, w, b, res, gam, bet = _linear_ln_inputs(700, n, k, 700, cuda_dev)
+    part, none16 = ops.linear_layernorm(x[300:437].contiguous(), w, b, gam, bet, res[300:437].clone(), 1e-12,
+                                        workspace=ws, want_h16=False)
+    assert none16 is None
+    assert torch.equal(part, outs[700][300:437])
+    ops.device_status(0)
+
+
+def test_linear_layernorm_rejects(cuda_dev):
+    from fastembed_b200 import ops
+    from fastembed_b200.capi import FeError
+    x, w, b, res, gam, bet = _linear_ln_inputs(64, 640, 64, 1, cuda_dev)
+    with pytest.raises(FeError):  # n = 640 is not a supported row width
+        ops.linear_layernorm(x, w, b, gam, bet, res, 1e-12)
+    x, w, b, res, gam, bet = _linear_ln_inputs(64, 512, 64, 1, cuda_dev)
+    small = torch.zeros(16, dtype=torch.uint8, device=cuda_dev)
+    with pytest.raises(FeError):  # workspace too small
+        ops.linear_layernorm(x, w, b, gam, bet, res, 1e-12, workspace=small)
+
+
 @pytest.mark.parametrize("mode", ["cls", "mean", "last"])
 def test_pool_l2_indices(cuda_dev, mode):
     from fastembed_b200 import ops
