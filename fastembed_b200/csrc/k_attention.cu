@@ -21,11 +21,17 @@
 //   warps 2-5  softmax: thread = query row; reads its S row (tcgen05.ld), masks keys past
 //              the sentence end, online max / sum, writes P (bf16) back over the first 64
 //              columns (tcgen05.st); one item later folds O into fp32 registers and,
-//              after a unit's last item, stores O / l.
+//              after a unit's last item, stores O / l.  (Folding O first would free the
+//              slot for the next S earlier, but then waits for this item's PV instead:
+//              measured slower with two slots per CTA.)
+// K and V tiles have separate full / empty barriers: a K slot is reloaded as soon as
+// the S two items back is done with it, without waiting for that item's PV.
 // Waits are bounded; on timeout the CTA records FE_ERR_DEVICE_TIMEOUT, drains what it
 // started and exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
+
+#include <mutex>
 
 #include "fe_common.cuh"
 #include "fe_internal.h"
@@ -38,13 +44,16 @@ constexpr int TQ = 128;
 constexpr int TK = 128;
 constexpr int Q_SLOTS = 2;
 constexpr int KV_SLOTS = 2;
-constexpr int kPrefetchItems = 8;               // key tiles requested into L2 ahead of the loads
-constexpr int kMaxUnits = 1024;                 // per-CTA unit list capacity
+constexpr int kLookahead = 4;                   // units grabbed (and prefetched into L2) ahead of the loads
+constexpr int kRing = 8;                        // grabbed units in flight to the MMA and softmax warps
+constexpr int kMaxBatch = 2048;                 // sentences per launch (prefix table in shared memory)
 constexpr int kCtasPerSm = 2;
+constexpr int kSchedSlots = 64;                 // work counters, one per launch in flight
 constexpr uint32_t Q_BYTES = TQ * HD * 2;       // 16 KB
 constexpr uint32_t KV_BYTES = 2 * TK * HD * 2;  // K then V, 32 KB
-constexpr uint32_t BAR_BYTES = 256;
-constexpr uint32_t SMEM_BYTES = 1024 + Q_SLOTS * Q_BYTES + KV_SLOTS * KV_BYTES + BAR_BYTES + 12 * kMaxUnits + 64;
+constexpr uint32_t BAR_BYTES = 512;
+constexpr uint32_t SMEM_BYTES =
+    1024 + Q_SLOTS * Q_BYTES + KV_SLOTS * KV_BYTES + BAR_BYTES + 16 * kRing + 4 * (kMaxBatch + 1) + 64;
 constexpr uint32_t TMEM_COLS = 256;  // two slots: S [0,128) -> P [0,64) + O [64,128)
 constexpr int kThreads = 192;
 
@@ -59,11 +68,14 @@ struct Unit {
     int start, len, q0, head, n_kv;
 };
 
-// A CTA's k-th valid unit: entry = {first row of the sentence, sentence length,
-// (head << 8) | query tile}.
-__device__ __forceinline__ Unit unit_at(const int3 *list, int k)
+// Per-launch work counters: [2 * slot] = next unit to hand out, [2 * slot + 1] = CTAs
+// finished; the last CTA of a launch sets both back to zero.
+__device__ unsigned g_attn_sched[2 * kSchedSlots];
+
+// A unit as passed through the ring: {first row of the sentence, sentence length (-1:
+// no more units), (head << 8) | query tile}.
+__device__ __forceinline__ Unit unit_of(const int4 e)
 {
-    const int3 e = list[k];
     Unit w;
     w.start = e.x;
     w.len = e.y;
@@ -75,7 +87,7 @@ __device__ __forceinline__ Unit unit_at(const int3 *list, int k)
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attn_varlen_tcgen05(const __grid_constant__ CUtensorMap tm_qkv, const int32_t *__restrict__ cu_seqlens,
-                        int batch, int heads, int qtiles, __nv_bfloat16 *__restrict__ out, float scale_log2,
+                        int batch, int heads, unsigned *sched, __nv_bfloat16 *__restrict__ out, float scale_log2,
                         int total_tokens, int head_major, int *status)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -85,22 +97,27 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     uint64_t *bars = reinterpret_cast<uint64_t *>(sKV + KV_SLOTS * KV_BYTES);
     uint64_t *q_full = bars;                  // [Q_SLOTS]
     uint64_t *q_empty = q_full + Q_SLOTS;     // [Q_SLOTS]
-    uint64_t *kv_full = q_empty + Q_SLOTS;    // [KV_SLOTS]
-    uint64_t *kv_empty = kv_full + KV_SLOTS;  // [KV_SLOTS]
-    uint64_t *s_full = kv_empty + KV_SLOTS;   // [2] S of a slot ready
+    uint64_t *k_full = q_empty + Q_SLOTS;     // [KV_SLOTS] K tile landed
+    uint64_t *k_empty = k_full + KV_SLOTS;    // [KV_SLOTS] S MMAs done with the K tile
+    uint64_t *v_full = k_empty + KV_SLOTS;    // [KV_SLOTS] V tile landed
+    uint64_t *v_empty = v_full + KV_SLOTS;    // [KV_SLOTS] PV MMAs done with the V tile
+    uint64_t *s_full = v_empty + KV_SLOTS;    // [2] S of a slot ready
     uint64_t *p_full = s_full + 2;            // [2] P of a slot written
     uint64_t *o_full = p_full + 2;            // [2] O of a slot ready
     uint64_t *slot_free = o_full + 2;         // [2] O of a slot consumed
     uint64_t *probe = slot_free + 2;          // [1]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(probe + 1);
+    uint64_t *unit_full = probe + 1;          // [kRing] a grabbed unit is in the ring slot
+    uint64_t *unit_empty = unit_full + kRing; // [kRing] the MMA and softmax warps have read it
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(unit_empty + kRing);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    int3 *ulist = reinterpret_cast<int3 *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES);
-    int *warp_tot = reinterpret_cast<int *>(ulist + kMaxUnits);
+    int *warp_tot = reinterpret_cast<int *>(tmem_slot + 2);  // [kThreads / 32]
+    // ring entries are written before an mbarrier arrive and read after the matching wait
+    int4 *ring = reinterpret_cast<int4 *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES);
+    int *upre = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES + 16 * kRing);  // [batch + 1]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int dim = heads * HD;
-    const int units = batch * qtiles * heads;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < Q_SLOTS; ++i) {
@@ -108,8 +125,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             mbar_init(&q_empty[i], 1);
         }
         for (int i = 0; i < KV_SLOTS; ++i) {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
@@ -118,6 +137,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             mbar_init(&slot_free[i], 4);  // one arrival per softmax warp
         }
         mbar_init(probe, 1);
+        for (int i = 0; i < kRing; ++i) {
+            mbar_init(&unit_full[i], 1);
+            mbar_init(&unit_empty[i], 5);  // the MMA thread and one arrival per softmax warp
+        }
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
@@ -127,51 +150,42 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         tmem_relinquish();
     }
 
-    // Unit u = blockIdx.x + i * gridDim.x is (sentence u / (H*QT), query tile (u / H) % QT,
-    // head u % H); keep, in order, those whose query tile starts inside the sentence.
+    // Units are handed out dynamically, in the order (sentence, query tile, head), from the
+    // launch's work counter.  upre[s] = number of units of sentences before s (each has
+    // ceil(len / 128) query tiles x heads units), so a unit index maps to its sentence by
+    // binary search.
     {
-        const int ncand = units > static_cast<int>(blockIdx.x) ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
         constexpr int nwarps = kThreads / 32;
-        int base = 0;
-        for (int c0 = 0; c0 < ncand; c0 += kThreads) {
-            const int ci = c0 + threadIdx.x;
-            bool valid = false;
-            int3 e = make_int3(0, 0, 0);
-            if (ci < ncand) {
-                const int u = blockIdx.x + ci * gridDim.x;
-                const int hh = u % heads;
-                const int t = (u / heads) % qtiles;
-                const int sidx = u / (heads * qtiles);
-                const int st = cu_seqlens[sidx];
-                const int ln = cu_seqlens[sidx + 1] - st;
-                valid = t * TQ < ln;
-                e = make_int3(st, ln, (hh << 8) | t);
+        int carry = 0;
+        for (int c0 = 0; c0 < batch; c0 += kThreads) {
+            const int i = c0 + threadIdx.x;
+            int v = 0;
+            if (i < batch) v = ((cu_seqlens[i + 1] - cu_seqlens[i] + TQ - 1) / TQ) * heads;
+            int x = v;  // inclusive warp scan
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
             }
-            const unsigned bal = __ballot_sync(0xffffffffu, valid);
-            if (lane == 0) warp_tot[warp] = __popc(bal);
+            if (lane == 31) warp_tot[warp] = x;
             __syncthreads();
-            int off = base, total = 0;
+            int off = carry, total = 0;
 #pragma unroll
             for (int w2 = 0; w2 < nwarps; ++w2) {
                 if (w2 < warp) off += warp_tot[w2];
                 total += warp_tot[w2];
             }
-            const int pos = off + __popc(bal & ((1u << lane) - 1));
-            if (valid && pos < kMaxUnits) ulist[pos] = e;
-            base += total;
+            if (i < batch) upre[i + 1] = off + x;
+            carry += total;
             __syncthreads();
         }
-        if (base > kMaxUnits) {
-            if (threadIdx.x == 0) report(status, DEV_BAD_INPUT);
-            base = 0;  // refuse the work rather than drop part of it
-        }
-        if (threadIdx.x == 0) warp_tot[nwarps] = base;
+        if (threadIdx.x == 0) upre[0] = 0;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int nlist = warp_tot[kThreads / 32];
+    const unsigned total_units = static_cast<unsigned>(upre[batch]);
 
     auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
         if (mbar_wait(bar, parity)) return true;
@@ -192,23 +206,52 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ------------------------------------------------ TMA producer
+            // ------------------------------------------------ TMA producer + unit scheduler
             uint32_t qn = 0, kvn = 0;
-            uint32_t q_armed = 0, kv_armed = 0, q_par = 0, kv_par = 0;
+            uint32_t q_armed = 0, kv_armed = 0, q_par = 0, kv_par = 0;  // kv_*: the K and V loads of a slot
             bool ok = true;
-            int pf_k = 0;           // next list entry to prefetch into L2
-            uint32_t pf_items = 0;  // key tiles prefetched so far
-            for (int k = 0; k < nlist && ok && !*abort_flag; ++k) {
-                const Unit w = unit_at(ulist, k);
-                while (pf_items < kvn + kPrefetchItems && pf_k < nlist) {
-                    const Unit pw = unit_at(ulist, pf_k++);
-                    prefetch_tile(0, pw.head, pw.start + pw.q0);
-                    for (int j = 0; j < pw.n_kv; ++j) {
-                        prefetch_tile(1, pw.head, pw.start + j * TK);
-                        prefetch_tile(2, pw.head, pw.start + j * TK);
+            uint32_t grabbed = 0, loaded = 0;  // units pushed into the ring / whose tiles were loaded
+            bool grab_done = false;
+            // Takes the next unit of the launch (or, past the last one, the end marker),
+            // pushes it into the ring and prefetches its tiles into L2.
+            auto grab = [&]() -> bool {
+                const unsigned g = atomicAdd(&sched[0], 1u);
+                int4 e = make_int4(0, -1, 0, 0);
+                if (g < total_units) {
+                    int lo = 0, hi = batch - 1;  // last sentence s with upre[s] <= g
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (upre[mid] <= static_cast<int>(g)) lo = mid;
+                        else hi = mid - 1;
                     }
-                    pf_items += pw.n_kv;
+                    const int rr = static_cast<int>(g) - upre[lo];
+                    const int st = cu_seqlens[lo];
+                    e = make_int4(st, cu_seqlens[lo + 1] - st, ((rr % heads) << 8) | (rr / heads), 0);
                 }
+                const int slot = grabbed % kRing;
+                if (!wait(&unit_empty[slot], ((grabbed / kRing) & 1) ^ 1)) return false;
+                ring[slot] = e;
+                mbar_arrive(&unit_full[slot]);
+                ++grabbed;
+                if (e.y < 0) {
+                    grab_done = true;
+                    return true;
+                }
+                const Unit pw = unit_of(e);
+                prefetch_tile(0, pw.head, pw.start + pw.q0);
+                for (int j = 0; j < pw.n_kv; ++j) {
+                    prefetch_tile(1, pw.head, pw.start + j * TK);
+                    prefetch_tile(2, pw.head, pw.start + j * TK);
+                }
+                return true;
+            };
+            while (ok && !*abort_flag) {
+                while (ok && !grab_done && grabbed < loaded + kLookahead) ok = grab();
+                if (!ok || loaded == grabbed) break;
+                const int4 e = ring[loaded % kRing];
+                ++loaded;
+                if (e.y < 0) break;
+                const Unit w = unit_of(e);
                 const int qs = qn % Q_SLOTS;
                 if (!(ok = wait(&q_empty[qs], ((qn / Q_SLOTS) & 1) ^ 1))) break;
                 mbar_arrive_expect_tx(&q_full[qs], Q_BYTES);
@@ -217,12 +260,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 q_par = (q_par & ~(1u << qs)) | (((qn / Q_SLOTS) & 1) << qs);
                 ++qn;
                 for (int j = 0; j < w.n_kv; ++j) {
+                    // K as soon as the S of two items back is done with the slot; V once its PV is
                     const int ks = kvn % KV_SLOTS;
-                    if (!(ok = wait(&kv_empty[ks], ((kvn / KV_SLOTS) & 1) ^ 1))) break;
+                    const uint32_t par = ((kvn / KV_SLOTS) & 1) ^ 1;
                     uint8_t *dst = sKV + ks * KV_BYTES;
-                    mbar_arrive_expect_tx(&kv_full[ks], KV_BYTES);
-                    load_tile(dst, &kv_full[ks], 1, w.head, w.start + j * TK);
-                    load_tile(dst + KV_BYTES / 2, &kv_full[ks], 2, w.head, w.start + j * TK);
+                    if (!(ok = wait(&k_empty[ks], par))) break;
+                    mbar_arrive_expect_tx(&k_full[ks], KV_BYTES / 2);
+                    load_tile(dst, &k_full[ks], 1, w.head, w.start + j * TK);
+                    if (!(ok = wait(&v_empty[ks], par))) {
+                        (void)mbar_wait(&k_full[ks], par ^ 1);  // the K load just started lands first
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&v_full[ks], KV_BYTES / 2);
+                    load_tile(dst + KV_BYTES / 2, &v_full[ks], 2, w.head, w.start + j * TK);
                     kv_armed |= 1u << ks;
                     kv_par = (kv_par & ~(1u << ks)) | (((kvn / KV_SLOTS) & 1) << ks);
                     ++kvn;
@@ -232,7 +282,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             for (int i = 0; i < Q_SLOTS; ++i)
                 if ((q_armed >> i) & 1) (void)mbar_wait(&q_full[i], (q_par >> i) & 1);
             for (int i = 0; i < KV_SLOTS; ++i)
-                if ((kv_armed >> i) & 1) (void)mbar_wait(&kv_full[i], (kv_par >> i) & 1);
+                if ((kv_armed >> i) & 1) {
+                    (void)mbar_wait(&k_full[i], (kv_par >> i) & 1);
+                    (void)mbar_wait(&v_full[i], (kv_par >> i) & 1);
+                }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -240,12 +293,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
             uint32_t qn = 0, kvn = 0, it = 0;
             bool issued = false, ok = true, have_pend = false;
-            uint32_t pend_it = 0, pend_ks = 0;
+            uint32_t pend_it = 0, pend_ks = 0, pend_kvn = 0;
             int pend_valid = 0;
             // O(slot) = P(slot) V for item `pit` (P from TMEM, V MN-major from smem)
-            auto issue_pv = [&](uint32_t pit, uint32_t pks, int pvalid) -> bool {
+            auto issue_pv = [&](uint32_t pit, uint32_t pks, uint32_t pkvn, int pvalid) -> bool {
                 const uint32_t b = pit & 1;
                 if (!wait(&p_full[b], (pit >> 1) & 1)) return false;
+                if (!wait(&v_full[pks], (pkvn / KV_SLOTS) & 1)) return false;
                 tc_fence_after();
                 const uint64_t v_desc = sdesc_sw128(smem_u32(sKV + pks * KV_BYTES + KV_BYTES / 2), TK * 128, 1024);
                 const int nks = (pvalid + 15) >> 4;
@@ -253,18 +307,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     umma_f16_ts(tmem + b * 128 + 64, tmem + b * 128 + ks * 8, v_desc + static_cast<uint64_t>(ks * 128),
                                 idesc_o, ks != 0 ? 1u : 0u);
                 umma_commit(&o_full[b]);
-                umma_commit(&kv_empty[pks]);
+                umma_commit(&v_empty[pks]);
                 return true;
             };
-            for (int k = 0; k < nlist && ok && !*abort_flag; ++k) {
-                const Unit w = unit_at(ulist, k);
+            for (uint32_t k = 0; ok && !*abort_flag; ++k) {
+                const int slot = k % kRing;
+                if (!(ok = wait(&unit_full[slot], (k / kRing) & 1))) break;
+                const int4 e = ring[slot];
+                mbar_arrive(&unit_empty[slot]);
+                if (e.y < 0) break;
+                const Unit w = unit_of(e);
                 const int qs = qn % Q_SLOTS;
                 if (!(ok = wait(&q_full[qs], (qn / Q_SLOTS) & 1))) break;
                 const uint64_t q_desc = sdesc_sw128(smem_u32(sQ + qs * Q_BYTES), 16, 1024);
                 for (int j = 0; j < w.n_kv; ++j) {
                     const uint32_t ks = kvn % KV_SLOTS;
                     const uint32_t b = it & 1;
-                    if (!(ok = wait(&kv_full[ks], (kvn / KV_SLOTS) & 1))) break;
+                    if (!(ok = wait(&k_full[ks], (kvn / KV_SLOTS) & 1))) break;
                     if (!(ok = wait(&slot_free[b], ((it >> 1) & 1) ^ 1))) break;
                     tc_fence_after();
                     const int valid = min(TK, w.len - j * TK);
@@ -277,18 +336,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                                     k_desc + static_cast<uint64_t>(kk * 2), idesc_s, kk != 0 ? 1u : 0u);
                     issued = true;
                     umma_commit(&s_full[b]);
+                    umma_commit(&k_empty[ks]);
                     if (j == w.n_kv - 1) umma_commit(&q_empty[qs]);
-                    if (have_pend && !(ok = issue_pv(pend_it, pend_ks, pend_valid))) break;
+                    if (have_pend && !(ok = issue_pv(pend_it, pend_ks, pend_kvn, pend_valid))) break;
                     have_pend = true;
                     pend_it = it;
                     pend_ks = ks;
+                    pend_kvn = kvn;
                     pend_valid = valid;
                     ++it;
                     ++kvn;
                 }
                 ++qn;
             }
-            if (ok && have_pend && !*abort_flag) ok = issue_pv(pend_it, pend_ks, pend_valid);
+            if (ok && have_pend && !*abort_flag) ok = issue_pv(pend_it, pend_ks, pend_kvn, pend_valid);
             if (issued) {
                 // all MMAs issued by this thread retire before TMEM is released
                 umma_commit(probe);
@@ -349,9 +410,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             return true;
         };
 
-        for (int k = 0; k < nlist && ok; ++k) {
+        for (uint32_t k = 0; ok; ++k) {
             if (*abort_flag) break;
-            const Unit w = unit_at(ulist, k);
+            const int slot = k % kRing;
+            if (!(ok = wait(&unit_full[slot], (k / kRing) & 1))) break;
+            const int4 e = ring[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&unit_empty[slot]);
+            if (e.y < 0) break;
+            const Unit w = unit_of(e);
             float m_run = -INFINITY, l_run = 0.f;
             __nv_bfloat16 *dst = nullptr;
             if (w.q0 + r < w.len) {
@@ -442,6 +509,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
+    // Every unit request of this CTA has been made; the launch's last CTA to get here
+    // returns the work counter to zero for the next launch that uses this slot.
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&sched[1], 1u) == gridDim.x - 1) {
+            atomicExch(&sched[0], 0u);
+            atomicExch(&sched[1], 0u);
+        }
+    }
 }
 
 }  // namespace
@@ -471,20 +547,38 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
         configured[dev] = true;
     }
     const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
-    const int qtiles = (max_len + TQ - 1) / TQ;
     const int ctas = kCtasPerSm * current_sm_count();
-    // Sentence offsets are absolute rows of qkv, so a long batch runs as chunks over the
-    // same tensor map, each small enough that a CTA's unit list fits kMaxUnits.
-    const int chunk = static_cast<int>(static_cast<int64_t>(kMaxUnits) * ctas / (static_cast<int64_t>(qtiles) * heads));
-    if (chunk < 1) {
-        *st = fail(FE_ERR_UNSUPPORTED, "attention: too many heads x query tiles per sentence");
+    // Each launch takes the next of kSchedSlots work counters (launches in flight at once
+    // on different streams use different counters); the counters live in this module.
+    static std::mutex sched_mu;
+    static unsigned *sched_base[64] = {};
+    static unsigned next_slot[64] = {};
+    if (dev >= 64) {
+        *st = fail(FE_ERR_UNSUPPORTED, "attention: device index above 63");
         return cudaSuccess;
     }
-    for (int b0 = 0; b0 < batch; b0 += chunk) {
-        const int nb = batch - b0 < chunk ? batch - b0 : chunk;
-        const int64_t units = static_cast<int64_t>(nb) * qtiles * heads;
-        const int grid = units < ctas ? static_cast<int>(units) : ctas;
-        attn_varlen_tcgen05<<<grid, kThreads, SMEM_BYTES, s>>>(tm, cu_seqlens + b0, nb, heads, qtiles,
+    unsigned *sched_dev = nullptr;
+    unsigned slot = 0;
+    {
+        std::lock_guard<std::mutex> lock(sched_mu);
+        if (!sched_base[dev]) {
+            void *p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_attn_sched);
+            if (e != cudaSuccess) return e;
+            sched_base[dev] = static_cast<unsigned *>(p);
+        }
+        sched_dev = sched_base[dev];
+        slot = next_slot[dev];
+        next_slot[dev] += static_cast<unsigned>((batch + kMaxBatch - 1) / kMaxBatch);
+    }
+    // Sentence offsets are absolute rows of qkv, so a long batch runs as chunks over the
+    // same tensor map, each small enough for the per-CTA prefix table.
+    for (int b0 = 0; b0 < batch; b0 += kMaxBatch) {
+        const int nb = batch - b0 < kMaxBatch ? batch - b0 : kMaxBatch;
+        const int64_t units_bound = static_cast<int64_t>(nb) * ((max_len + TQ - 1) / TQ) * heads;
+        const int grid = units_bound < ctas ? static_cast<int>(units_bound) : ctas;
+        unsigned *sched = sched_dev + 2 * (slot++ % kSchedSlots);
+        attn_varlen_tcgen05<<<grid, kThreads, SMEM_BYTES, s>>>(tm, cu_seqlens + b0, nb, heads, sched,
                                                                static_cast<__nv_bfloat16 *>(out), scale_log2,
                                                                static_cast<int>(total_tokens), head_major ? 1 : 0,
                                                                current_device_status_word());

@@ -335,14 +335,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 // CTA's epilogue drains its own 128 accumulator rows and reports back to the leader.
 // Pair p owns tiles p, p + npairs, ...; tile t covers rows (t / n_tiles) * 256 and
 // columns (t % n_tiles) * 256.
-constexpr int P_STAGES = 6;
 constexpr int P_BN = 256;
 constexpr uint32_t P_HALF_BYTES = 128 * BK * 2;        // 16 KB: 128 rows x 64 bf16
 constexpr uint32_t P_STAGE_BYTES = 2 * P_HALF_BYTES;   // this CTA's x rows + W rows
 constexpr uint32_t P_TMEM_COLS = 2 * P_BN;
-constexpr uint32_t P_RING_BYTES = P_STAGES * P_STAGE_BYTES;
-constexpr uint32_t P_EPI_BYTES = kEpiWarps * 2 * kStageBufBytes;
-constexpr uint32_t P_SMEM_BYTES = 1024 + P_RING_BYTES + P_EPI_BYTES + 256;
+
+// Pair-kernel configuration: ring stages and epilogue warps (4, or 8 = two per TMEM
+// lane quarter, each draining 128 of the 256 accumulator columns).
+template <int STAGES, int EPI_WARPS>
+struct PairCfg {
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int COLS = P_BN / (EPI_WARPS / 4);
+    static constexpr uint32_t RING = STAGES * P_STAGE_BYTES;
+    static constexpr uint32_t EPI = EPI_WARPS * 2 * kStageBufBytes;
+    static constexpr uint32_t SMEM = 1024 + RING + EPI + 256;
+    static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "epilogue warps");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
 
 // TMA producer of a pair (lane 0 of warp 0 in both CTAs).
 template <int STAGES>
@@ -439,19 +448,20 @@ __device__ __forceinline__ void pair_mma(uint8_t *ring, uint64_t *full, uint64_t
     }
 }
 
-template <bool OUT_BF16>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <bool OUT_BF16, int P_STAGES, int EPI_WARPS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EPI_WARPS>::THREADS, 1)
     linear_tcgen05_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_y, int M, int N, int K,
                         const float *__restrict__ bias, const float *__restrict__ residual, int epi, int *status)
 {
+    using Cfg = PairCfg<P_STAGES, EPI_WARPS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
-    uint8_t *epi_buf = smem + P_RING_BYTES;
-    uint64_t *full = reinterpret_cast<uint64_t *>(epi_buf + P_EPI_BYTES);  // used in the leader
-    uint64_t *empty = full + P_STAGES;                                     // both CTAs
-    uint64_t *acc_full = empty + P_STAGES;                                 // both CTAs [2]
+    uint8_t *epi_buf = smem + Cfg::RING;
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi_buf + Cfg::EPI);  // used in the leader
+    uint64_t *empty = full + P_STAGES;                                  // both CTAs
+    uint64_t *acc_full = empty + P_STAGES;                              // both CTAs [2]
     uint64_t *acc_empty = acc_full + 2;                                    // used in the leader [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -473,7 +483,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 2 * kEpiWarps);  // one arrival per epilogue warp of either CTA
+            mbar_init(&acc_empty[b], 2 * EPI_WARPS);  // one arrival per epilogue warp of either CTA
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -500,9 +510,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             pair_mma<P_STAGES>(ring, full, empty, acc_full, acc_empty, tmem_base, pair, npairs, num_tiles, k_iters,
                                abort_flag, status);
     } else {
-        // ---------------- epilogue (warps 2..5 of both CTAs)
+        // ---------------- epilogue (warps 2.. of both CTAs): warp w drains TMEM lanes
+        // 32 * (w % 4) (the lane-quarter rule), columns [h * COLS, (h + 1) * COLS), h = (w - 2) / 4
+        constexpr int COLS = Cfg::COLS;
         const int q = warp & 3;
-        uint8_t *bufs = epi_buf + q * 2 * kStageBufBytes;
+        const int h = (warp - 2) >> 2;
+        uint8_t *bufs = epi_buf + (warp - 2) * 2 * kStageBufBytes;
         const uint32_t leader_acc_empty[2] = {map_to_rank(&acc_empty[0], 0), map_to_rank(&acc_empty[1], 0)};
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -516,10 +529,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const int m0 = (tile / n_tiles) * 256 + static_cast<int>(rank) * 128;
-            const int n0 = (tile % n_tiles) * P_BN;
+            const int n0 = (tile % n_tiles) * P_BN + h * COLS;
             const int row = m0 + q * 32 + lane;
-            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN;
-            drain_accumulator<P_BN, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN + h * COLS;
+            drain_accumulator<COLS, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
                                               lane);
             tc_fence_before();
             __syncwarp();
@@ -948,16 +961,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
     }
 }
 
+// 6 stages x 4 epilogue warps: on the bge-large projections (K = 1024) 5 x 8 and 4 x 8
+// measured 1-5 % slower, the deeper ring mattering more than the wider epilogue.
+constexpr int kPairStages = 6;
+constexpr int kPairEpiWarps = 4;
+
 template <bool OUT_BF16>
 cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N, int K,
                         const float *bias, const float *residual, int epi, int *status, cudaStream_t s)
 {
+    using Cfg = PairCfg<kPairStages, kPairEpiWarps>;
+    auto kern = linear_tcgen05_pair<OUT_BF16, kPairStages, kPairEpiWarps>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(linear_tcgen05_pair<OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             P_SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
@@ -965,8 +984,7 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
     int pairs = current_sm_count() / 2;
     if (pairs > tiles) pairs = tiles;
     if (pairs < 1) pairs = 1;
-    linear_tcgen05_pair<OUT_BF16><<<2 * pairs, kThreads, P_SMEM_BYTES, s>>>(tx, tw, ty, M, N, K, bias, residual, epi,
-                                                                           status);
+    kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM, s>>>(tx, tw, ty, M, N, K, bias, residual, epi, status);
     return cudaGetLastError();
 }
 

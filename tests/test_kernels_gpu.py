@@ -124,6 +124,27 @@ def test_attention_varlen(cuda_dev, lens, heads):
     ops.device_status(0)
 
 
+def test_attention_many_sentences_and_repeat(cuda_dev):
+    """More sentences than one launch takes (2048): the batch runs as chunks, each
+    handing out its units from its own work counter; a repeat is bit-identical."""
+    from fastembed_b200 import ops
+    rng = np.random.default_rng(4)
+    lens = rng.integers(0, 40, size=2300).tolist()
+    lens[5] = 300  # one multi-tile sentence among many short and empty ones
+    heads = 2
+    g = torch.Generator(device=cuda_dev).manual_seed(4)
+    T = sum(lens)
+    qkv = torch.randn(T, 3 * heads * 64, device=cuda_dev, generator=g).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    out1 = ops.attention_varlen(qkv, cu, max(lens), heads)
+    out2 = ops.attention_varlen(qkv, cu, max(lens), heads)
+    ref = _attn_ref(qkv, lens, heads)
+    torch.cuda.synchronize()
+    assert float((out1.float() - ref).abs().max()) < 2e-2
+    assert torch.equal(out1, out2)
+    ops.device_status(0)
+
+
 def test_attention_sharp_softmax(cuda_dev):
     """Large scores (near one-hot rows) exercise the online max / rescale across key tiles."""
     from fastembed_b200 import ops
