@@ -63,6 +63,7 @@ _SIGS = {
     "fe_attention_varlen_bf16": ([vp, vp, i32, i32, i32, i32, vp, i64, vp], C.c_int),
     "fe_embed_layernorm": ([vp, vp, i32, i64, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, vp], C.c_int),
     "fe_layernorm_dual": ([vp, vp, vp, vp, vp, vp, i64, i32, f32, vp], C.c_int),
+    "fe_attention_varlen_gqa_bf16": ([vp, vp, i32, i32, i32, i32, i32, i32, f32, vp, i64, vp], C.c_int),
     "fe_linear_layernorm_workspace_bytes": ([i64, i64, C.POINTER(sz)], C.c_int),
     "fe_linear_layernorm_bf16": ([vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, vp, sz, vp], C.c_int),
     "fe_pool_l2": ([vp, vp, i32, i32, C.c_int, vp, vp], C.c_int),

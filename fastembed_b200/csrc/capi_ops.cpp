@@ -177,6 +177,29 @@ fe_status fe_attention_varlen_bf16(const void *qkv, const int32_t *cu_seqlens, i
     return done(e, "fe_attention_varlen_bf16");
 }
 
+fe_status fe_attention_varlen_gqa_bf16(const void *qkv, const int32_t *cu_seqlens, int32_t batch, int32_t max_len,
+                                       int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t causal, float scale,
+                                       void *out, int64_t total_tokens, fe_stream_t stream)
+{
+    if (batch < 0 || max_len < 0 || q_heads <= 0 || kv_heads <= 0 || total_tokens < 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_gqa_bf16: bad shape");
+    if (q_heads % kv_heads != 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_gqa_bf16: q_heads must be a multiple of kv_heads");
+    if (head_dim != 128 && head_dim != 256)
+        return fail(FE_ERR_UNSUPPORTED, "fe_attention_varlen_gqa_bf16: head_dim must be 128 or 256");
+    if (max_len > 65536 || batch > 1 << 24 || q_heads > 1024)
+        return fail(FE_ERR_UNSUPPORTED, "fe_attention_varlen_gqa_bf16: batch, heads or max_len too large");
+    if (batch == 0 || total_tokens == 0) return FE_OK;
+    if (!qkv || !cu_seqlens || !out) return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_gqa_bf16: null pointer");
+    if (!aligned16(qkv) || !aligned16(out))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_attention_varlen_gqa_bf16: pointers must be 16-byte aligned");
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_attention_wide(qkv, cu_seqlens, batch, max_len, q_heads, kv_heads, head_dim, causal != 0,
+                                              scale, out, total_tokens, reinterpret_cast<cudaStream_t>(stream), &st);
+    if (st != FE_OK) return st;
+    return done(e, "fe_attention_varlen_gqa_bf16");
+}
+
 fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int32_t batch, int64_t total_tokens,
                              const float *word, const float *pos, const float *type, const float *gamma,
                              const float *beta, int32_t dim, int32_t vocab, int32_t max_pos, float eps, float *h32,

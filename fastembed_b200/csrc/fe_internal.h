@@ -71,6 +71,11 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
                                     int max_len, int heads, int head_dim, void *out,
                                     int64_t total_tokens, bool head_major, cudaStream_t s,
                                     fe_status *st);
+// Grouped-query attention for head_dim 128 / 256: qkv [T, (q_heads + 2 kv_heads) * head_dim]
+// (Q heads, then K heads, then V heads), out [T, q_heads * head_dim].
+cudaError_t launch_attention_wide(const void *qkv, const int32_t *cu_seqlens, int batch, int max_len, int q_heads,
+                                  int kv_heads, int head_dim, bool causal, float scale, void *out,
+                                  int64_t total_tokens, cudaStream_t s, fe_status *st);
 cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
                                    const float *word, const float *pos, const float *type,
                                    const float *g, const float *b, int dim, int vocab,

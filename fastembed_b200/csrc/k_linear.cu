@@ -1099,6 +1099,7 @@ size_t round_up_256(size_t v) { return (v + 255) & ~size_t(255); }
 // launches running at once could each hold SMs that the other's waiting pairs need.
 std::mutex g_ln_mu;
 cudaEvent_t g_ln_last[64] = {};
+cudaStream_t g_ln_last_stream[64] = {};  // stream of that launch: no wait needed on the same stream
 // Next epoch of each statistics workspace (keyed by its address); 0 is never used, so
 // a zero-filled workspace holds no valid partial.
 std::unordered_map<const void *, unsigned> g_ln_epoch;
@@ -1178,7 +1179,7 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
     unsigned &ep = g_ln_epoch[stats];
     if (++ep == 0) ep = 1;
     p.epoch = ep;
-    if (order && g_ln_last[dev]) {
+    if (order && g_ln_last[dev] && g_ln_last_stream[dev] != s) {
         cudaError_t e = cudaStreamWaitEvent(s, g_ln_last[dev], 0);
         if (e != cudaSuccess) return e;
     }
@@ -1195,6 +1196,7 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
             if (e != cudaSuccess) return e;
         }
         e = cudaEventRecord(g_ln_last[dev], s);
+        g_ln_last_stream[dev] = s;
     }
     return e;
 }

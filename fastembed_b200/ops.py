@@ -107,6 +107,17 @@ def attention_varlen(qkv, cu_seqlens, max_len, heads, head_dim=64):
     return out
 
 
+def attention_gqa(qkv, cu_seqlens, max_len, q_heads, kv_heads, head_dim, causal, scale=None):
+    """Grouped-query varlen attention (head_dim 128 / 256): qkv [T, (Hq + 2 Hkv) * hd] bf16."""
+    _cuda(qkv, cu_seqlens)
+    T = qkv.shape[0]
+    scale = head_dim ** -0.5 if scale is None else scale
+    out = torch.empty(T, q_heads * head_dim, dtype=torch.bfloat16, device=qkv.device)
+    call("fe_attention_varlen_gqa_bf16", _p(qkv), _p(cu_seqlens), cu_seqlens.numel() - 1, max_len, q_heads, kv_heads,
+         head_dim, 1 if causal else 0, scale, _p(out), T, _s(qkv))
+    return out
+
+
 def embed_layernorm(ids, cu_seqlens, word, pos, type_, gamma, beta, eps):
     _cuda(ids, cu_seqlens, word, pos, type_, gamma, beta)
     T = ids.numel()

@@ -148,6 +148,17 @@ fe_status fe_linear_bf16(const void *x, const void *w, const float *bias, const 
 fe_status fe_attention_varlen_bf16(const void *qkv, const int32_t *cu_seqlens, int32_t batch,
                                    int32_t max_len, int32_t heads, int32_t head_dim, void *out,
                                    int64_t total_tokens, fe_stream_t stream);
+/* Grouped-query variable-length attention for head_dim 128 or 256 (the Qwen3 and Gemma3
+ * shapes; these models are not in the reference, whose attention is
+ * src/ops/cpu/cpu_attention_ops.cpp:33-85 with one key-value head per query head).
+ * qkv is bf16 [total_tokens, (q_heads + 2*kv_heads)*head_dim]: the query heads, then the
+ * key heads, then the value heads; query head h reads key-value head
+ * h / (q_heads / kv_heads).  out [total_tokens, q_heads*head_dim] bf16 =
+ * softmax(Q K^T * scale) V per sentence; causal != 0 keeps key j for query i only when
+ * j <= i.  Requires q_heads % kv_heads == 0. */
+fe_status fe_attention_varlen_gqa_bf16(const void *qkv, const int32_t *cu_seqlens, int32_t batch, int32_t max_len,
+                                       int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t causal, float scale,
+                                       void *out, int64_t total_tokens, fe_stream_t stream);
 /* Fused embedding sum + LayerNorm over a packed batch: x_t = word[id_t] +
  * pos[t - start(s)] + type[0]; writes LN(x) as fp32 (h32) and bf16 (h16).
  * Replaces src/sentence_transformers_impl.cpp:30-44, :155-194.  Out-of-range ids

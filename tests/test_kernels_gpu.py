@@ -145,6 +145,47 @@ def test_attention_many_sentences_and_repeat(cuda_dev):
     ops.device_status(0)
 
 
+def _attn_gqa_ref(qkv, lens, hq, hkv, hd, causal, scale):
+    out = torch.zeros(qkv.shape[0], hq * hd, device=qkv.device)
+    kc, vc = hq * hd, (hq + hkv) * hd
+    s = 0
+    for L in lens:
+        if L == 0:
+            continue
+        q = qkv[s:s + L, :kc].float().view(L, hq, hd).transpose(0, 1)
+        k = qkv[s:s + L, kc:vc].float().view(L, hkv, hd).transpose(0, 1).repeat_interleave(hq // hkv, 0)
+        v = qkv[s:s + L, vc:].float().view(L, hkv, hd).transpose(0, 1).repeat_interleave(hq // hkv, 0)
+        sc = q @ k.transpose(1, 2) * scale
+        if causal:
+            sc = sc.masked_fill(torch.ones(L, L, dtype=torch.bool, device=qkv.device).triu(1), float("-inf"))
+        out[s:s + L] = (torch.softmax(sc, -1) @ v).transpose(0, 1).reshape(L, hq * hd)
+        s += L
+    return out
+
+
+@pytest.mark.parametrize("hd,hq,hkv,causal,lens", [
+    (128, 16, 8, True, [1, 7, 128, 129, 300, 64, 511]),
+    (128, 4, 4, False, [200, 3, 128, 255]),
+    (128, 8, 2, True, [1024, 40]),
+    (256, 3, 1, False, [1, 8, 100, 256, 257, 33]),
+    (256, 4, 2, True, [130, 12, 384]),
+])
+def test_attention_gqa(cuda_dev, hd, hq, hkv, causal, lens):
+    """Grouped-query attention for head_dim 128 / 256 against fp32 torch: causal and
+    bidirectional, ragged lengths, several 128-key items per unit (O rescaled in TMEM)."""
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(sum(lens) + hd + hq)
+    T = sum(lens)
+    qkv = (torch.randn(T, (hq + 2 * hkv) * hd, device=cuda_dev, generator=g) * 1.5).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    out = ops.attention_gqa(qkv, cu, max(lens), hq, hkv, hd, causal)
+    ref = _attn_gqa_ref(qkv, lens, hq, hkv, hd, causal, hd ** -0.5)
+    torch.cuda.synchronize()
+    # P rounded to bf16 (2^-9 relative per weight), O to bf16: 3e-2 abs on unit-scale V
+    assert float((out.float() - ref).abs().max()) < 3e-2
+    ops.device_status(0)
+
+
 def test_attention_sharp_softmax(cuda_dev):
     """Large scores (near one-hot rows) exercise the online max / rescale across key tiles."""
     from fastembed_b200 import ops
