@@ -14,7 +14,8 @@ LIB_PATH = os.path.join(PKG, "lib", "libfastembed_b200.so")
 FE_OK = 0
 STATUS = {0: "FE_OK", 1: "FE_ERR_INVALID_ARGUMENT", 2: "FE_ERR_CUDA", 3: "FE_ERR_OUT_OF_MEMORY",
           4: "FE_ERR_UNSUPPORTED", 5: "FE_ERR_DEVICE_TIMEOUT", 6: "FE_ERR_IO", 7: "FE_ERR_NOT_FOUND"}
-EPI = {"none": 0, "bias": 1, "bias_gelu": 2, "bias_relu": 3, "bias_swish": 4, "bias_residual": 5}
+EPI = {"none": 0, "bias": 1, "bias_gelu": 2, "bias_relu": 3, "bias_swish": 4, "bias_residual": 5, "swiglu": 6,
+       "geglu": 7}
 DTYPE = {"f32": 0, "bf16": 1}
 POOL = {"cls": 0, "mean": 1, "last": 2}
 ACT = {"gelu": 0, "relu": 1, "swish": 2}
@@ -66,6 +67,10 @@ _SIGS = {
     "fe_attention_varlen_gqa_bf16": ([vp, vp, i32, i32, i32, i32, i32, i32, f32, vp, i64, vp], C.c_int),
     "fe_linear_layernorm_workspace_bytes": ([i64, i64, C.POINTER(sz)], C.c_int),
     "fe_linear_layernorm_bf16": ([vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, vp, sz, vp], C.c_int),
+    "fe_embed_scale": ([vp, i64, vp, i32, i32, f32, vp, vp], C.c_int),
+    "fe_rms_norm_rows": ([vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),
+    "fe_rms_sandwich": ([vp, vp, vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),
+    "fe_qk_norm_rope_bf16": ([vp, vp, i32, i64, i32, i32, i32, vp, vp, i32, f32, f32, vp], C.c_int),
     "fe_pool_l2": ([vp, vp, i32, i32, C.c_int, vp, vp], C.c_int),
     "fe_engine_create": ([C.POINTER(EncoderConfig), C.c_int, C.POINTER(vp)], C.c_int),
     "fe_engine_destroy": ([vp], C.c_int),

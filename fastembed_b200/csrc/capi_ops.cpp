@@ -134,15 +134,19 @@ fe_status fe_linear_bf16(const void *x, const void *w, const float *bias, const 
     if (m < 0 || n <= 0 || k <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: bad shape");
     if (k % 8 != 0 || n % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: k and n must be multiples of 8");
     if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_linear_bf16: size too large");
-    if (epilogue < FE_EPI_NONE || epilogue > FE_EPI_BIAS_RESIDUAL)
+    if (epilogue < FE_EPI_NONE || epilogue > FE_EPI_GEGLU)
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: unknown epilogue");
+    const bool glu = epilogue == FE_EPI_SWIGLU || epilogue == FE_EPI_GEGLU;
+    if (glu && (n % 128 != 0 || y_dtype != FE_DTYPE_BF16))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: gated epilogues need n % 128 == 0 and bf16 output");
     if (y_dtype != FE_DTYPE_F32 && y_dtype != FE_DTYPE_BF16)
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: unknown output dtype");
     if (epilogue == FE_EPI_BIAS_RESIDUAL && y_dtype != FE_DTYPE_F32)
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: the residual epilogue writes fp32");
     if (m == 0) return FE_OK;
     if (!x || !w || !y) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: null pointer");
-    if (epilogue != FE_EPI_NONE && !bias) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: epilogue needs a bias");
+    if (epilogue != FE_EPI_NONE && !glu && !bias)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: epilogue needs a bias");
     if (epilogue == FE_EPI_BIAS_RESIDUAL && !residual)
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: residual epilogue needs a residual");
     if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias && !aligned16(bias)) ||
@@ -267,6 +271,60 @@ fe_status fe_linear_layernorm_bf16(const void *x, const void *w, const float *bi
                                                 reinterpret_cast<cudaStream_t>(stream), &st);
     if (st != FE_OK) return st;
     return done(e, "fe_linear_layernorm_bf16");
+}
+
+static bool rms_dim_ok(int32_t dim) { return supported_row_dim(dim) && dim != 128; }
+
+fe_status fe_embed_scale(const int32_t *ids, int64_t total_tokens, const float *word, int32_t vocab, int32_t dim,
+                         float scale, float *h32, fe_stream_t stream)
+{
+    if (total_tokens < 0 || vocab <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_scale: bad shape");
+    if (!rms_dim_ok(dim)) return fail(FE_ERR_UNSUPPORTED, "fe_embed_scale: unsupported dim");
+    if (total_tokens == 0) return FE_OK;
+    if (!ids || !word || !h32) return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_scale: null pointer");
+    return done(fe::launch_embed_scale(ids, total_tokens, word, vocab, dim, scale, h32,
+                                       reinterpret_cast<cudaStream_t>(stream)),
+                "fe_embed_scale");
+}
+
+fe_status fe_rms_norm_rows(const float *x, const float *w, int32_t one_plus, float eps, int64_t rows, int32_t dim,
+                           float *o32, void *o16, fe_stream_t stream)
+{
+    if (rows < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_norm_rows: bad shape");
+    if (!rms_dim_ok(dim)) return fail(FE_ERR_UNSUPPORTED, "fe_rms_norm_rows: unsupported dim");
+    if (rows == 0) return FE_OK;
+    if (!x || !w || (!o32 && !o16)) return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_norm_rows: null pointer");
+    return done(fe::launch_rms_norm_rows(x, w, one_plus != 0, eps, rows, dim, o32, o16,
+                                         reinterpret_cast<cudaStream_t>(stream)),
+                "fe_rms_norm_rows");
+}
+
+fe_status fe_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, int32_t one_plus,
+                          float eps, int64_t rows, int32_t dim, float *o32, void *o16, fe_stream_t stream)
+{
+    if (rows < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_sandwich: bad shape");
+    if (!rms_dim_ok(dim)) return fail(FE_ERR_UNSUPPORTED, "fe_rms_sandwich: unsupported dim");
+    if (rows == 0) return FE_OK;
+    if (!y || !w_post || !h32 || !w_next || (!o32 && !o16))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_sandwich: null pointer");
+    return done(fe::launch_rms_sandwich(y, w_post, h32, w_next, one_plus != 0, eps, rows, dim, o32, o16,
+                                        reinterpret_cast<cudaStream_t>(stream)),
+                "fe_rms_sandwich");
+}
+
+fe_status fe_qk_norm_rope_bf16(void *qkv, const int32_t *cu_seqlens, int32_t batch, int64_t total_tokens,
+                               int32_t q_heads, int32_t kv_heads, int32_t head_dim, const float *q_w, const float *k_w,
+                               int32_t one_plus, float eps, float theta, fe_stream_t stream)
+{
+    if (batch < 0 || total_tokens < 0 || q_heads <= 0 || kv_heads <= 0 || !(theta > 1.0f))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_qk_norm_rope_bf16: bad shape");
+    if (head_dim != 128 && head_dim != 256) return fail(FE_ERR_UNSUPPORTED, "fe_qk_norm_rope_bf16: head_dim 128 or 256");
+    if (total_tokens == 0) return FE_OK;
+    if (batch == 0 || !qkv || !cu_seqlens || !q_w || !k_w)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_qk_norm_rope_bf16: null pointer or no sentences");
+    return done(fe::launch_qk_norm_rope(qkv, cu_seqlens, batch, total_tokens, q_heads, kv_heads, head_dim, q_w, k_w,
+                                        one_plus != 0, eps, theta, reinterpret_cast<cudaStream_t>(stream)),
+                "fe_qk_norm_rope_bf16");
 }
 
 fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, int32_t dim, fe_pooling mode,

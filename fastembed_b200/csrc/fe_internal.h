@@ -76,6 +76,17 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
 cudaError_t launch_attention_wide(const void *qkv, const int32_t *cu_seqlens, int batch, int max_len, int q_heads,
                                   int kv_heads, int head_dim, bool causal, float scale, void *out,
                                   int64_t total_tokens, cudaStream_t s, fe_status *st);
+// Row kernels of the RMSNorm / RoPE encoders (k_decoder.cu); one_plus selects the
+// (1 + w) weight form.  dim in {256, 384, 512, 768, 1024, 1536, 2048}.
+cudaError_t launch_embed_scale(const int32_t *ids, int64_t total, const float *word, int vocab, int dim, float scale,
+                               float *h32, cudaStream_t s);
+cudaError_t launch_rms_norm_rows(const float *x, const float *w, bool one_plus, float eps, int64_t rows, int dim,
+                                 float *o32, void *o16, cudaStream_t s);
+cudaError_t launch_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, bool one_plus,
+                                float eps, int64_t rows, int dim, float *o32, void *o16, cudaStream_t s);
+cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t total, int q_heads, int kv_heads,
+                                int head_dim, const float *q_w, const float *k_w, bool one_plus, float eps, float theta,
+                                cudaStream_t s);
 cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
                                    const float *word, const float *pos, const float *type,
                                    const float *g, const float *b, int dim, int vocab,

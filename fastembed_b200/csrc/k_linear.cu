@@ -37,7 +37,7 @@ constexpr int kEpiWarps = 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, mma, 4 epilogue warps
 constexpr uint32_t kStageBufBytes = 32 * 128;  // one warp's 32-row x 128 B store slab
 
-enum Epi : int { E_NONE = 0, E_BIAS = 1, E_GELU = 2, E_RELU = 3, E_SWISH = 4, E_RESID = 5 };
+enum Epi : int { E_NONE = 0, E_BIAS = 1, E_GELU = 2, E_RELU = 3, E_SWISH = 4, E_RESID = 5, E_SWIGLU = 6, E_GEGLU = 7 };
 
 template <int BN>
 struct Cfg {
@@ -71,6 +71,52 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
                                                   const float *__restrict__ residual, int epi,
                                                   const CUtensorMap *tm_y, uint8_t *bufs, int &pp, int lane)
 {
+    if constexpr (OUT_BF16) {
+        if (epi == E_SWIGLU || epi == E_GEGLU) {
+            // Gated MLP: W rows interleave 32 gate and 32 up rows, so each 64-column block of
+            // the accumulator gives 32 outputs act(gate) * up; 128 accumulator columns fill one
+            // 64-column bf16 slab of y, which has N / 2 columns.
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 128) {
+                float o[64];
+#pragma unroll
+                for (int hb = 0; hb < 2; ++hb) {
+                    uint32_t g[32], u[32];
+                    tmem_ld_x32(t_row + c + 64 * hb, g);
+                    tmem_ld_x32(t_row + c + 64 * hb + 32, u);
+                    tmem_wait_ld_regs(g);
+                    tmem_wait_ld_regs(u);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float a = __uint_as_float(g[j]);
+                        const float ga = epi == E_SWIGLU ? a / (1.0f + __expf(-a)) : gelu_tanh_fast(a);
+                        o[32 * hb + j] = ga * __uint_as_float(u[j]);
+                    }
+                }
+                uint8_t *buf = bufs + pp * kStageBufBytes;
+                if (lane == 0) bulk_wait_read<1>();
+                __syncwarp();
+                uint8_t *rowp = buf + lane * 128;
+#pragma unroll
+                for (int c16 = 0; c16 < 8; ++c16) {
+                    uint4 w;
+                    w.x = pack_bf16x2(o[c16 * 8 + 0], o[c16 * 8 + 1]);
+                    w.y = pack_bf16x2(o[c16 * 8 + 2], o[c16 * 8 + 3]);
+                    w.z = pack_bf16x2(o[c16 * 8 + 4], o[c16 * 8 + 5]);
+                    w.w = pack_bf16x2(o[c16 * 8 + 6], o[c16 * 8 + 7]);
+                    *reinterpret_cast<uint4 *>(rowp + ((c16 ^ (lane & 7)) << 4)) = w;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(tm_y, buf, (n0 + c) / 2, store_row);
+                    bulk_commit();
+                }
+                pp ^= 1;
+            }
+            return;
+        }
+    }
     constexpr int CHUNK = OUT_BF16 ? 64 : 32;  // output columns per 128-byte slab
 #pragma unroll 1
     for (int c = 0; c < BN; c += CHUNK) {
@@ -1056,11 +1102,13 @@ cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
     // 256-row pair tiles once there are at least two of them per 256 columns
     const bool use_pair = pair_mode_enabled() && BN == 256 && m >= 512;
     const bool out_bf16 = y_dtype == FE_DTYPE_BF16;
+    const bool glu = epilogue == E_SWIGLU || epilogue == E_GEGLU;
+    const int64_t ny = glu ? n / 2 : n;  // y columns
     CUtensorMap tx, tw, ty;
     fe_status r = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, k, k, BM, BK);
     if (r == FE_OK) r = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, k, k, BN, BK);
     if (r == FE_OK)
-        r = out_bf16 ? make_tmap_2d(&ty, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, n, n, 32, 64)
+        r = out_bf16 ? make_tmap_2d(&ty, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, ny, ny, 32, 64)
                      : make_tmap_2d(&ty, y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, n, n, 32, 32);
     if (r != FE_OK) {
         *st = r;

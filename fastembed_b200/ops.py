@@ -92,7 +92,8 @@ def linear_bf16(x, w, bias=None, residual=None, epilogue="none", out_dtype="bf16
     _cuda(x, w, bias, residual)
     m, k = x.shape
     n = w.shape[0]
-    y = torch.empty(m, n, dtype=torch.bfloat16 if out_dtype == "bf16" else torch.float32, device=x.device)
+    ny = n // 2 if epilogue in ("swiglu", "geglu") else n
+    y = torch.empty(m, ny, dtype=torch.bfloat16 if out_dtype == "bf16" else torch.float32, device=x.device)
     call("fe_linear_bf16", _p(x), _p(w), _p(bias), _p(residual), _p(y), m, n, k, EPI[epilogue],
          DTYPE[out_dtype], _s(x))
     return y
@@ -156,6 +157,42 @@ def linear_layernorm(x, w, bias, gamma, beta, h32, eps, workspace=None, want_h16
     call("fe_linear_layernorm_bf16", _p(x), _p(w), _p(bias), _p(gamma), _p(beta), _p(h32), _p(h16), m, n, k, eps,
          _p(workspace), workspace.numel(), _s(x))
     return h32, h16
+
+
+def embed_scale(ids, word, scale):
+    _cuda(ids, word)
+    T = ids.numel()
+    h32 = torch.empty(T, word.shape[1], dtype=torch.float32, device=ids.device)
+    call("fe_embed_scale", _p(ids), T, _p(word), word.shape[0], word.shape[1], scale, _p(h32), _s(ids))
+    return h32
+
+
+def rms_norm_rows(x, w, eps, one_plus=False):
+    _cuda(x, w)
+    rows, D = x.shape
+    o32 = torch.empty_like(x)
+    o16 = torch.empty(rows, D, dtype=torch.bfloat16, device=x.device)
+    call("fe_rms_norm_rows", _p(x), _p(w), 1 if one_plus else 0, eps, rows, D, _p(o32), _p(o16), _s(x))
+    return o32, o16
+
+
+def rms_sandwich(y, w_post, h32, w_next, eps, one_plus=True):
+    """h32 += RMSNorm(y; w_post) in place; returns (RMSNorm(h32; w_next) fp32, bf16)."""
+    _cuda(y, w_post, h32, w_next)
+    rows, D = y.shape
+    o32 = torch.empty_like(y)
+    o16 = torch.empty(rows, D, dtype=torch.bfloat16, device=y.device)
+    call("fe_rms_sandwich", _p(y), _p(w_post), _p(h32), _p(w_next), 1 if one_plus else 0, eps, rows, D, _p(o32),
+         _p(o16), _s(y))
+    return o32, o16
+
+
+def qk_norm_rope(qkv, cu_seqlens, q_heads, kv_heads, head_dim, q_w, k_w, eps, theta, one_plus=False):
+    """In place on qkv [T, (Hq + 2 Hkv) * hd] bf16."""
+    _cuda(qkv, cu_seqlens, q_w, k_w)
+    call("fe_qk_norm_rope_bf16", _p(qkv), _p(cu_seqlens), cu_seqlens.numel() - 1, qkv.shape[0], q_heads, kv_heads,
+         head_dim, _p(q_w), _p(k_w), 1 if one_plus else 0, eps, theta, _s(qkv))
+    return qkv
 
 
 def pool_l2(h, cu_seqlens, mode="cls"):

@@ -52,7 +52,12 @@ typedef enum fe_epilogue {
     FE_EPI_BIAS_GELU = 2,     /* y = gelu_tanh(x W^T + b)           */
     FE_EPI_BIAS_RELU = 3,     /* y = relu(x W^T + b)                */
     FE_EPI_BIAS_SWISH = 4,    /* y = swish(x W^T + b)               */
-    FE_EPI_BIAS_RESIDUAL = 5  /* y = x W^T + b + residual (fp32)    */
+    FE_EPI_BIAS_RESIDUAL = 5, /* y = x W^T + b + residual (fp32)    */
+    /* Gated MLP (not in the reference; Qwen3 / Gemma3 shapes): W has n rows that
+     * alternate 32 gate rows and 32 up rows; y has n/2 columns, bf16, y = act(x Wg^T) * (x Wu^T)
+     * with act = silu or gelu_tanh; no bias.  n % 128 == 0. */
+    FE_EPI_SWIGLU = 6,
+    FE_EPI_GEGLU = 7
 } fe_epilogue;
 
 typedef enum fe_dtype { FE_DTYPE_F32 = 0, FE_DTYPE_BF16 = 1 } fe_dtype;
@@ -189,6 +194,24 @@ fe_status fe_linear_layernorm_workspace_bytes(int64_t m, int64_t n, size_t *byte
 fe_status fe_linear_layernorm_bf16(const void *x, const void *w, const float *bias, const float *gamma,
                                    const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
                                    float eps, void *workspace, size_t workspace_bytes, fe_stream_t stream);
+/* ---- RMSNorm / RoPE encoders (Qwen3, Gemma3 shapes; not in the reference) ----
+ * dim in {256, 384, 512, 768, 1024, 1536, 2048}; one_plus != 0 uses (1 + w) as the
+ * norm weight (Gemma3), else w (Qwen3).  All statistics in fp32. */
+/* h32[t] = word[ids[t]] * scale (fp32 [total, dim]). */
+fe_status fe_embed_scale(const int32_t *ids, int64_t total_tokens, const float *word, int32_t vocab, int32_t dim,
+                         float scale, float *h32, fe_stream_t stream);
+/* out = x / sqrt(mean(x^2) + eps) * w, written as fp32 (o32) and / or bf16 (o16). */
+fe_status fe_rms_norm_rows(const float *x, const float *w, int32_t one_plus, float eps, int64_t rows, int32_t dim,
+                           float *o32, void *o16, fe_stream_t stream);
+/* h32 += RMSNorm(y; w_post), then out = RMSNorm(h32; w_next) as fp32 and / or bf16. */
+fe_status fe_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, int32_t one_plus,
+                          float eps, int64_t rows, int32_t dim, float *o32, void *o16, fe_stream_t stream);
+/* In place on qkv [total, (q_heads + 2*kv_heads)*head_dim] bf16: per-head RMSNorm of the
+ * query (q_w) and key (k_w) heads, then the rotate-half rotary embedding with inverse
+ * frequencies theta^(-2i/head_dim) at positions 0.. within each sentence.  head_dim 128 / 256. */
+fe_status fe_qk_norm_rope_bf16(void *qkv, const int32_t *cu_seqlens, int32_t batch, int64_t total_tokens,
+                               int32_t q_heads, int32_t kv_heads, int32_t head_dim, const float *q_w, const float *k_w,
+                               int32_t one_plus, float eps, float theta, fe_stream_t stream);
 /* Per-sentence pooling + L2 normalisation of packed hidden states h [total, dim]
  * into out [batch, dim].  Replaces src/sentence_transformers_impl.cpp:289-341. */
 fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, int32_t dim,

@@ -380,3 +380,97 @@ def test_fp32_mha_matches_oracle_reference_inputs(cuda_dev, oracle_lib):
         t = lambda v: torch.tensor(v, device=cuda_dev)
         got = ops.mha_f32(t(x), t(w), t(w), t(w), t(b), t(b), t(b), H, D).cpu().numpy()
         assert np.abs(got - ref).max() < 1e-3
+
+
+# ------------------------------------ RMSNorm / RoPE / gated-MLP encoders (Qwen3, Gemma3)
+def _interleave32(gate, up):
+    """Gate / up weights -> the gated epilogue's layout: 32 gate rows, 32 up rows, ..."""
+    F, K = gate.shape
+    return torch.stack([gate.view(F // 32, 32, K), up.view(F // 32, 32, K)], 1).reshape(2 * F, K).contiguous()
+
+
+@pytest.mark.parametrize("pair", ["1", "0"])
+@pytest.mark.parametrize("m,F,k", [(600, 3072, 1024), (77, 1152, 768), (1000, 128, 64)])
+@pytest.mark.parametrize("epi", ["swiglu", "geglu"])
+def test_linear_gated(cuda_dev, monkeypatch, m, F, k, epi, pair):
+    from fastembed_b200 import ops
+    monkeypatch.setenv("FE_LINEAR_PAIR", pair)
+    g = torch.Generator(device=cuda_dev).manual_seed(m + F + k)
+    x = torch.randn(m, k, device=cuda_dev, generator=g).to(torch.bfloat16)
+    wg = (torch.randn(F, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    wu = (torch.randn(F, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    y = ops.linear_bf16(x, _interleave32(wg, wu), None, None, epi, "bf16")
+    a = x.float() @ wg.float().T
+    act = torch.nn.functional.silu(a) if epi == "swiglu" else torch.nn.functional.gelu(a, approximate="tanh")
+    ref = act * (x.float() @ wu.float().T)
+    torch.cuda.synchronize()
+    assert y.shape == (m, F)
+    assert _rel_err(y, ref) < 1e-2  # bf16 output rounding and the fast exp / tanh
+    ops.device_status(0)
+
+
+def _rms_ref(x, w, eps, one_plus):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * ((1 + w) if one_plus else w)
+
+
+@pytest.mark.parametrize("D,one_plus", [(1024, False), (768, True), (256, True)])
+def test_rms_rows_and_sandwich(cuda_dev, D, one_plus):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(D)
+    x = torch.randn(517, D, device=cuda_dev, generator=g) * 3 + 0.5
+    w = torch.randn(D, device=cuda_dev, generator=g) * 0.2 + (0 if one_plus else 1)
+    o32, o16 = ops.rms_norm_rows(x, w, 1e-6, one_plus)
+    ref = _rms_ref(x, w, 1e-6, one_plus)
+    assert float((o32 - ref).abs().max()) < 1e-4
+    assert torch.equal(o16, o32.to(torch.bfloat16))
+    y = torch.randn(517, D, device=cuda_dev, generator=g) * 5
+    h = torch.randn(517, D, device=cuda_dev, generator=g)
+    w2 = torch.randn(D, device=cuda_dev, generator=g) * 0.2
+    h_ref = h + _rms_ref(y, w, 1e-6, one_plus)
+    s32, s16 = ops.rms_sandwich(y, w, h, w2, 1e-6, one_plus)
+    assert float((h - h_ref).abs().max()) < 1e-4
+    assert float((s32 - _rms_ref(h_ref, w2, 1e-6, one_plus)).abs().max()) < 1e-4
+    assert torch.equal(s16, s32.to(torch.bfloat16))
+
+
+def _rope_ref(x, pos, theta):
+    hd = x.shape[-1]
+    inv = 1.0 / (theta ** (torch.arange(0, hd, 2, device=x.device).float() / hd))
+    ang = pos[:, None].float() * inv[None]
+    cos, sin = torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
+    rot = torch.cat([-x[..., hd // 2:], x[..., :hd // 2]], -1)
+    return x * cos[:, None] + rot * sin[:, None]
+
+
+@pytest.mark.parametrize("hd,hq,hkv,theta,one_plus", [(128, 16, 8, 1e6, False), (256, 3, 1, 1e4, True)])
+def test_qk_norm_rope(cuda_dev, hd, hq, hkv, theta, one_plus):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(hd + hq)
+    lens = [1, 130, 7, 600]
+    T = sum(lens)
+    qkv = (torch.randn(T, (hq + 2 * hkv) * hd, device=cuda_dev, generator=g) * 2).to(torch.bfloat16)
+    qw = torch.randn(hd, device=cuda_dev, generator=g) * 0.3 + (0 if one_plus else 1)
+    kw = torch.randn(hd, device=cuda_dev, generator=g) * 0.3 + (0 if one_plus else 1)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    pos = torch.cat([torch.arange(L, device=cuda_dev) for L in lens])
+    src = qkv.float()
+    q = src[:, :hq * hd].view(T, hq, hd)
+    k = src[:, hq * hd:(hq + hkv) * hd].view(T, hkv, hd)
+    q_ref = _rope_ref(_rms_ref(q, qw, 1e-6, one_plus), pos, theta).reshape(T, -1)
+    k_ref = _rope_ref(_rms_ref(k, kw, 1e-6, one_plus), pos, theta).reshape(T, -1)
+    out = ops.qk_norm_rope(qkv.clone(), cu, hq, hkv, hd, qw, kw, 1e-6, theta, one_plus).float()
+    torch.cuda.synchronize()
+    scale = float(max(q_ref.abs().max(), k_ref.abs().max()))
+    assert float((out[:, :hq * hd] - q_ref).abs().max()) < 1e-2 * scale  # bf16 output
+    assert float((out[:, hq * hd:(hq + hkv) * hd] - k_ref).abs().max()) < 1e-2 * scale
+    assert torch.equal(out[:, (hq + hkv) * hd:], src[:, (hq + hkv) * hd:])  # V untouched
+    ops.device_status(0)
+
+
+def test_embed_scale_exact(cuda_dev):
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(9)
+    word = torch.randn(5000, 768, device=cuda_dev, generator=g)
+    ids = torch.randint(0, 5000, (1234,), device=cuda_dev, generator=g, dtype=torch.int32)
+    h = ops.embed_scale(ids, word, 27.712812)
+    assert torch.equal(h, word[ids.long()] * torch.tensor(27.712812, device=cuda_dev))
