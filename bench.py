@@ -37,6 +37,21 @@ from fastembed_b200 import workload as W  # noqa: E402
 METRIC = "sentences/s bge-large b=256 L=512 @1/2/4/8 B200; attn+GEMM % TC peak"
 UNIT = "sentences/s"
 WORKLOAD = "bge-large"
+# --workload: the headline bge-large shape (default) or the Qwen3 / Gemma3 shapes, which
+# the reference has no path for (no CPU baseline; informational lines)
+DESCRIPTIONS = {
+    "bge-large": "bge-large shape (24L, D1024, 16x64 heads, F4096 GELU, post-LN, CLS+L2), 256 sentences per GPU, "
+                 "lognormal lengths median 96 sigma 0.6 in [8,512], packed without padding, seeded N(0,0.02) weights",
+    "qwen3-0.6b": "Qwen3-0.6B shape (28L, D1024, 16q/8kv x 128 heads, causal, RoPE 1e6, F3072 SwiGLU, pre-RMSNorm, "
+                  "last-token+L2), 128 sentences per GPU, lengths U[64,1024], packed, seeded N(0,0.02) weights",
+    "gemma-300m": "Gemma-300M shape (24L, D768, 3q/1kv x 256 heads, bidirectional, RoPE 1e4/1e6, F1152 GeGLU, "
+                  "sandwich RMSNorm, mean+L2), 512 sentences per GPU, lengths U[8,256], packed, seeded N(0,0.02) "
+                  "weights",
+}
+
+
+def workload_shape(name):
+    return W.SHAPES[name] if name in W.SHAPES else W.RMS_SHAPES[name]
 
 
 def peaks():
@@ -50,8 +65,12 @@ def peaks():
 
 # ------------------------------------------------------------------ workload
 def global_batch(shape, world, per_gpu=None):
-    lengths = W.sample_lengths(shape, batch=(per_gpu or shape.batch) * world, seed=1)
-    ids, _ = W.sample_ids(shape, lengths, seed=1, pad_to=int(lengths.max()))
+    if hasattr(shape, "family"):
+        lengths = W.sample_rms_lengths(shape, batch=(per_gpu or shape.batch) * world, seed=1)
+        ids = W.sample_rms_ids(shape, lengths, seed=1)
+    else:
+        lengths = W.sample_lengths(shape, batch=(per_gpu or shape.batch) * world, seed=1)
+        ids, _ = W.sample_ids(shape, lengths, seed=1, pad_to=int(lengths.max()))
     order = np.argsort(-lengths, kind="stable")
     return lengths[order], ids[order]
 
@@ -224,12 +243,13 @@ def ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
-    shape = W.SHAPES[WORKLOAD]
+    shape = workload_shape(args.workload)
+    rms = hasattr(shape, "family")
     lengths_all, ids_all = global_batch(shape, world, args.batch)
     lo, hi = rank_slice(shape, lengths_all, world, rank)
     lengths = np.ascontiguousarray(lengths_all[lo:hi])
     ids = np.ascontiguousarray(ids_all[lo:hi])
-    weights = W.make_weights(shape)
+    weights = W.make_rms_weights(shape) if rms else W.make_weights(shape)
     eng = ops.Engine(shape, local)
     eng.load_weights(weights)
 
@@ -286,7 +306,10 @@ def ours(args):
     attn_tflops = attn_flops * args.steps / (attn_ms / 1e3) / 1e12 if attn_ms else 0.0
     # attention is HBM-bound at these lengths: its algorithmic bytes are one read of Q, K, V
     # and one write of O per layer, all bf16
-    attn_bytes = shape.layers * tokens_local * 4 * shape.hidden * 2
+    if rms:  # Q, K, V and O of every head, bf16
+        attn_bytes = shape.layers * tokens_local * (2 * shape.q_heads + 2 * shape.kv_heads) * shape.head_dim * 2
+    else:
+        attn_bytes = shape.layers * tokens_local * 4 * shape.hidden * 2
     attn_gbs = attn_bytes * args.steps / (attn_ms / 1e3) / 1e9 if attn_ms else 0.0
 
     # ---- end to end through the host-buffer C ABI entry point
@@ -305,29 +328,29 @@ def ours(args):
     d2h = sum_over_ranks(float(lengths.size * shape.hidden * 4))
 
     cpu_base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not rms:
         v, info = run_cpu_reference(shape, lengths_all, ids_all, weights, steps=1, warmup=0, budget_total_s=20.0)
         cpu_base = {"value": v, "unit": UNIT, "cores": info["cores"], "kind": info["kind"], "sample": info["sample"]}
 
     if rank == 0:
         traffic = None
         tpath = os.path.join(ROOT, "profiles", "linear_tcgen05_pair_bge-large.md")
-        if os.path.exists(tpath):
+        if os.path.exists(tpath) and not rms:
             with open(tpath) as f:
                 for ln in f:
                     if ln.startswith("traffic_bytes_per_launch:"):
                         traffic = int(ln.split(":")[1])
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if args.workload == WORKLOAD else f"sentences/s {args.workload} @1/2/4/8 B200",
+            "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "bge-large shape (24L, D1024, 16x64 heads, F4096 GELU, post-LN, CLS+L2), "
-                                   "256 sentences per GPU, lognormal lengths median 96 sigma 0.6 in [8,512], "
-                                   "packed without padding, seeded N(0,0.02) weights",
+            "config": {"workload": DESCRIPTIONS[args.workload],
                        "global_batch": int(sentences), "valid_tokens_per_step": int(tokens),
                        "tokens_per_s": tokens / (ms_per_step / 1e3),
                        "parallelism": f"replica dp{world}, FLOP-balanced contiguous slices, no collective",
-                       "l2": "inputs larger than L2: 0.6 GB of bf16 weights and ~0.7 GB of activations per step"},
+                       "l2": "inputs larger than L2: the bf16 weights and the activations of a step are each "
+                             "several times the 126 MB L2"},
             "roofline": {"bound": "tensor", "kernel": "linear_tcgen05 (all QKV/out/FFN projections)",
                          "achieved": gemm_tflops, "peak": sustained_tf, "unit": "TFLOP/s",
                          "frac": gemm_tflops / sustained_tf, "peak_kind": f"bf16 sustained, {peak_kind}",
@@ -347,6 +370,7 @@ def ours(args):
             "gpu_launches": int(launches),
             "clocks": clock_info,
             "cpu_baseline": cpu_base,
+            **({"cpu_baseline_note": "the reference has no Qwen3 / Gemma3 forward"} if rms else {}),
         }
         print(json.dumps(line), flush=True)
     eng.close()
@@ -363,11 +387,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=None, help="sentences per GPU (default 256)")
+    ap.add_argument("--batch", type=int, default=None, help="sentences per GPU (default: the workload's)")
+    ap.add_argument("--workload", choices=sorted(DESCRIPTIONS), default=WORKLOAD,
+                    help="bge-large (the headline) or the Qwen3 / Gemma3 shapes (informational)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
+        if args.workload != WORKLOAD:
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference has no Qwen3 / Gemma3 forward"}))
+            return 0
         return reference_arm(args)
     return ours(args)
 

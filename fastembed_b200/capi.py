@@ -34,6 +34,17 @@ class EncoderConfig(C.Structure):
                 ("pooling", C.c_int32)]
 
 
+class RmsEncoderConfig(C.Structure):
+    _fields_ = [("family", C.c_int32), ("vocab_size", C.c_int32), ("hidden", C.c_int32), ("layers", C.c_int32),
+                ("q_heads", C.c_int32), ("kv_heads", C.c_int32), ("head_dim", C.c_int32),
+                ("intermediate", C.c_int32), ("max_position", C.c_int32), ("rms_norm_eps", C.c_float),
+                ("rope_theta", C.c_float), ("rope_theta_local", C.c_float), ("full_attention_every", C.c_int32),
+                ("query_scale", C.c_float), ("pooling", C.c_int32)]
+
+
+FAMILY = {"bert": 0, "qwen3": 1, "gemma3": 2}
+
+
 class EngineStats(C.Structure):
     _fields_ = [("launches", C.c_int64), ("gemm_launches", C.c_int64), ("tokens", C.c_int64),
                 ("gemm_ms", C.c_double), ("attention_ms", C.c_double), ("other_ms", C.c_double),
@@ -73,6 +84,7 @@ _SIGS = {
     "fe_qk_norm_rope_bf16": ([vp, vp, i32, i64, i32, i32, i32, vp, vp, i32, f32, f32, vp], C.c_int),
     "fe_pool_l2": ([vp, vp, i32, i32, C.c_int, vp, vp], C.c_int),
     "fe_engine_create": ([C.POINTER(EncoderConfig), C.c_int, C.POINTER(vp)], C.c_int),
+    "fe_engine_create_rms": ([C.POINTER(RmsEncoderConfig), C.c_int, C.POINTER(vp)], C.c_int),
     "fe_engine_destroy": ([vp], C.c_int),
     "fe_engine_set_weight": ([vp, C.c_char_p, vp, sz, C.c_int], C.c_int),
     "fe_engine_load_safetensors": ([vp, C.c_char_p], C.c_int),

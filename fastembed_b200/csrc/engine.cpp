@@ -18,6 +18,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -78,6 +79,17 @@ struct Slot {
     size_t offset;
     size_t count;
     bool bf16;
+    // gated-MLP weights: 0 = contiguous; 1 / 2 = this [F, row] matrix goes to the even /
+    // odd 32-row blocks of the interleaved [2F, row] gate-up matrix
+    int interleave = 0;
+    size_t row = 0;
+};
+
+// One layer of a pre-RMSNorm rotary encoder (Qwen3 / Gemma3 shapes).
+struct RLayer {
+    DevBuf wqkv, wo, wgu, wd;                        // bf16 [(Hq+2Hkv)hd, D], [D, Hq hd], [2F, D], [D, F]
+    DevBuf q_norm, k_norm;                           // fp32 [hd]
+    DevBuf in_norm, post_attn_norm, pre_ff_norm, post_ff_norm;  // fp32 [D]
 };
 
 enum Cat { CAT_GEMM = 0, CAT_ATTN = 1, CAT_OTHER = 2 };
@@ -86,6 +98,11 @@ enum Cat { CAT_GEMM = 0, CAT_ATTN = 1, CAT_OTHER = 2 };
 
 struct fe_engine {
     fe_encoder_config cfg{};
+    int family = FE_FAMILY_BERT;
+    fe_rms_encoder_config rc{};  // RMSNorm families
+    std::vector<RLayer> rlayers;
+    DevBuf final_norm, zero_bias, hfin;  // hfin: final-norm output [T, D] fp32 (RMSNorm families)
+    DevBuf staging16;  // bf16 conversion buffer of interleaved uploads
     int device = 0;
     cudaStream_t stream = nullptr;
     std::mutex mu;
@@ -310,6 +327,243 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
     return FE_OK;
 }
 
+// ---------------------------------------------------------------- RMSNorm families
+bool is_gemma(const fe_engine *e) { return e->family == FE_FAMILY_GEMMA3; }
+
+fe_status alloc_weights_rms(fe_engine *e)
+{
+    const fe_rms_encoder_config &c = e->rc;
+    const size_t D = c.hidden, F = c.intermediate, hd = c.head_dim;
+    const size_t QKV = static_cast<size_t>(c.q_heads + 2 * c.kv_heads) * hd, AO = static_cast<size_t>(c.q_heads) * hd;
+    auto f32 = [&](DevBuf &b, size_t n) { return b.ensure(n * sizeof(float)); };
+    auto b16 = [&](DevBuf &b, size_t n) { return b.ensure(n * sizeof(__nv_bfloat16)); };
+    FE_TRY_CUDA(f32(e->word, static_cast<size_t>(c.vocab_size) * D));
+    FE_TRY_CUDA(f32(e->final_norm, D));
+    FE_TRY_CUDA(f32(e->zero_bias, std::max(D, 2 * F)));
+    FE_TRY_CUDA(cudaMemset(e->zero_bias.p, 0, std::max(D, 2 * F) * sizeof(float)));
+    e->slots["embed_tokens.weight"] = {&e->word, 0, static_cast<size_t>(c.vocab_size) * D, false};
+    e->slots["norm.weight"] = {&e->final_norm, 0, D, false};
+    e->rlayers.resize(c.layers);
+    for (int l = 0; l < c.layers; ++l) {
+        RLayer &L = e->rlayers[l];
+        FE_TRY_CUDA(b16(L.wqkv, QKV * D));
+        FE_TRY_CUDA(b16(L.wo, D * AO));
+        FE_TRY_CUDA(b16(L.wgu, 2 * F * D));
+        FE_TRY_CUDA(b16(L.wd, D * F));
+        FE_TRY_CUDA(f32(L.q_norm, hd));
+        FE_TRY_CUDA(f32(L.k_norm, hd));
+        FE_TRY_CUDA(f32(L.in_norm, D));
+        FE_TRY_CUDA(f32(L.post_attn_norm, D));
+        const std::string p = "layers." + std::to_string(l) + ".";
+        e->slots[p + "self_attn.q_proj.weight"] = {&L.wqkv, 0, AO * D, true};
+        e->slots[p + "self_attn.k_proj.weight"] = {&L.wqkv, AO * D, c.kv_heads * hd * D, true};
+        e->slots[p + "self_attn.v_proj.weight"] = {&L.wqkv, (AO + c.kv_heads * hd) * D, c.kv_heads * hd * D, true};
+        e->slots[p + "self_attn.o_proj.weight"] = {&L.wo, 0, D * AO, true};
+        e->slots[p + "self_attn.q_norm.weight"] = {&L.q_norm, 0, hd, false};
+        e->slots[p + "self_attn.k_norm.weight"] = {&L.k_norm, 0, hd, false};
+        Slot gate{&L.wgu, 0, F * D, true};
+        gate.interleave = 1;
+        gate.row = D;
+        Slot up = gate;
+        up.interleave = 2;
+        e->slots[p + "mlp.gate_proj.weight"] = gate;
+        e->slots[p + "mlp.up_proj.weight"] = up;
+        e->slots[p + "mlp.down_proj.weight"] = {&L.wd, 0, D * F, true};
+        e->slots[p + "input_layernorm.weight"] = {&L.in_norm, 0, D, false};
+        e->slots[p + "post_attention_layernorm.weight"] = {&L.post_attn_norm, 0, D, false};
+        if (is_gemma(e)) {
+            FE_TRY_CUDA(f32(L.pre_ff_norm, D));
+            FE_TRY_CUDA(f32(L.post_ff_norm, D));
+            e->slots[p + "pre_feedforward_layernorm.weight"] = {&L.pre_ff_norm, 0, D, false};
+            e->slots[p + "post_feedforward_layernorm.weight"] = {&L.post_ff_norm, 0, D, false};
+        }
+    }
+    for (auto &kv : e->slots) e->loaded[kv.first] = false;
+    return FE_OK;
+}
+
+fe_status ensure_activations_rms(fe_engine *e, int64_t T)
+{
+    if (T <= e->cap_tokens) return FE_OK;
+    const fe_rms_encoder_config &c = e->rc;
+    const int64_t cap = std::max<int64_t>(T, 128);
+    const size_t D = c.hidden, F = c.intermediate, hd = c.head_dim;
+    FE_TRY_CUDA(e->h32.ensure(cap * D * 4));
+    FE_TRY_CUDA(e->h16.ensure(cap * D * 2));
+    FE_TRY_CUDA(e->qkv.ensure(cap * (c.q_heads + 2 * c.kv_heads) * hd * 2));
+    FE_TRY_CUDA(e->attn.ensure(cap * c.q_heads * hd * 2));
+    FE_TRY_CUDA(e->y32.ensure(cap * D * 4));
+    FE_TRY_CUDA(e->ff.ensure(cap * F * 2));
+    FE_TRY_CUDA(e->hfin.ensure(cap * D * 4));
+    e->cap_tokens = cap;
+    return FE_OK;
+}
+
+// Theta of layer l (Gemma3: every full_attention_every-th layer is a global layer).
+float layer_theta(const fe_rms_encoder_config &c, int l)
+{
+    if (c.full_attention_every <= 0) return c.rope_theta;
+    return (l + 1) % c.full_attention_every == 0 ? c.rope_theta : c.rope_theta_local;
+}
+
+fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const int32_t *cu_host, int batch,
+                      float *out, cudaStream_t s)
+{
+    const fe_rms_encoder_config &c = e->rc;
+    const int64_t T = cu_host[batch];
+    int max_len = 0;
+    for (int b = 0; b < batch; ++b) {
+        const int L = cu_host[b + 1] - cu_host[b];
+        if (L < 0) return fail(FE_ERR_INVALID_ARGUMENT, "cu_seqlens must be non-decreasing");
+        if (L > c.max_position) return fail(FE_ERR_INVALID_ARGUMENT, "sequence length exceeds max_position");
+        if (is_gemma(e) && L > 1024)
+            return fail(FE_ERR_UNSUPPORTED, "Gemma3 shapes: sentences up to 1024 tokens (no sliding-window mask)");
+        max_len = std::max(max_len, L);
+    }
+    if (cu_host[0] != 0) return fail(FE_ERR_INVALID_ARGUMENT, "cu_seqlens[0] must be 0");
+    FE_TRY(ensure_activations_rms(e, T));
+    e->stats.launches = 0;
+    e->stats.gemm_launches = 0;
+    e->stats.tokens = T;
+    e->ev_used = 0;
+    const int64_t D = c.hidden, F = c.intermediate, hd = c.head_dim;
+    const int64_t QKV = (c.q_heads + 2 * c.kv_heads) * hd, AO = static_cast<int64_t>(c.q_heads) * hd;
+    const bool gemma = is_gemma(e);
+    double gemm_flops = 0, attn_flops = 0;
+    for (int b = 0; b < batch; ++b) {
+        const double L = cu_host[b + 1] - cu_host[b];
+        gemm_flops += c.layers * 2.0 * L * (static_cast<double>(D) * QKV + AO * D + 3.0 * D * F);
+        const double pairs = gemma ? L * L : L * (L + 1) / 2;  // causal: the lower triangle
+        attn_flops += c.layers * 4.0 * pairs * AO;
+    }
+    e->stats.gemm_flops = gemm_flops;
+    e->stats.attention_flops = attn_flops;
+    if (T == 0) {
+        if (batch > 0) FE_TRY_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * batch * D, s));
+        return FE_OK;
+    }
+    float *h32 = e->h32.as<float>(), *y32 = e->y32.as<float>();
+    void *x16 = e->h16.p, *qkv = e->qkv.p, *attn = e->attn.p, *ff = e->ff.p;
+    const float eps = c.rms_norm_eps;
+    const float qscale = c.query_scale > 0.f ? c.query_scale : 1.0f / sqrtf(static_cast<float>(hd));
+    auto gemm = [&](const void *x, const DevBuf &w, const float *bias, const float *res, void *y, int64_t n, int64_t k,
+                    int epi, int dtype) -> fe_status {
+        Scope sc(e, CAT_GEMM, s);
+        fe_status st = FE_OK;
+        cudaError_t err = fe::launch_linear_bf16(x, w.p, bias, res, y, T, n, k, epi, dtype, s, &st);
+        if (st != FE_OK) return st;
+        return fe::check_cuda(err, "linear");
+    };
+    {
+        Scope sc(e, CAT_OTHER, s);
+        // Gemma3 scales the embeddings by sqrt(hidden) (rounded to fp32); Qwen3 does not
+        const float escale = gemma ? static_cast<float>(std::sqrt(static_cast<double>(D))) : 1.0f;
+        FE_TRY_CUDA(fe::launch_embed_scale(ids, T, e->word.as<float>(), c.vocab_size, static_cast<int>(D), escale, h32, s));
+    }
+    {
+        Scope sc(e, CAT_OTHER, s);
+        FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, e->rlayers[0].in_norm.as<float>(), gemma, eps, T, static_cast<int>(D),
+                                             nullptr, x16, s));
+    }
+    float *fin = e->hfin.as<float>();  // the final-norm output (fp32) for pooling
+    for (int l = 0; l < c.layers; ++l) {
+        const RLayer &L = e->rlayers[l];
+        const bool last = l + 1 == c.layers;
+        FE_TRY(gemm(x16, L.wqkv, nullptr, nullptr, qkv, QKV, D, FE_EPI_NONE, FE_DTYPE_BF16));
+        {
+            Scope sc(e, CAT_OTHER, s);
+            FE_TRY_CUDA(fe::launch_qk_norm_rope(qkv, cu, batch, T, c.q_heads, c.kv_heads, static_cast<int>(hd),
+                                                L.q_norm.as<float>(), L.k_norm.as<float>(), gemma, eps,
+                                                layer_theta(c, l), s));
+        }
+        {
+            Scope sc(e, CAT_ATTN, s);
+            fe_status st = FE_OK;
+            cudaError_t err = fe::launch_attention_wide(qkv, cu, batch, max_len, c.q_heads, c.kv_heads,
+                                                        static_cast<int>(hd), !gemma, qscale, attn, T, s, &st);
+            if (st != FE_OK) return st;
+            FE_TRY_CUDA(err);
+        }
+        const float *next_norm = last ? e->final_norm.as<float>() : e->rlayers[l + 1].in_norm.as<float>();
+        if (!gemma) {
+            // x <- x + attn Wo^T (residual in the GEMM epilogue, in place); then the post-attention norm
+            FE_TRY(gemm(attn, L.wo, e->zero_bias.as<float>(), h32, h32, D, AO, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32));
+            {
+                Scope sc(e, CAT_OTHER, s);
+                FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, L.post_attn_norm.as<float>(), false, eps, T,
+                                                     static_cast<int>(D), nullptr, x16, s));
+            }
+            FE_TRY(gemm(x16, L.wgu, nullptr, nullptr, ff, 2 * F, D, FE_EPI_SWIGLU, FE_DTYPE_BF16));
+            FE_TRY(gemm(ff, L.wd, e->zero_bias.as<float>(), h32, h32, D, F, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32));
+            {
+                Scope sc(e, CAT_OTHER, s);
+                FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, next_norm, false, eps, T, static_cast<int>(D),
+                                                     last ? fin : nullptr, last ? nullptr : x16, s));
+            }
+        } else {
+            // x <- x + rms(attn Wo^T), then the pre-FFN norm, in one row kernel
+            FE_TRY(gemm(attn, L.wo, nullptr, nullptr, y32, D, AO, FE_EPI_NONE, FE_DTYPE_F32));
+            {
+                Scope sc(e, CAT_OTHER, s);
+                FE_TRY_CUDA(fe::launch_rms_sandwich(y32, L.post_attn_norm.as<float>(), h32, L.pre_ff_norm.as<float>(),
+                                                    true, eps, T, static_cast<int>(D), nullptr, x16, s));
+            }
+            FE_TRY(gemm(x16, L.wgu, nullptr, nullptr, ff, 2 * F, D, FE_EPI_GEGLU, FE_DTYPE_BF16));
+            FE_TRY(gemm(ff, L.wd, nullptr, nullptr, y32, D, F, FE_EPI_NONE, FE_DTYPE_F32));
+            {
+                Scope sc(e, CAT_OTHER, s);
+                FE_TRY_CUDA(fe::launch_rms_sandwich(y32, L.post_ff_norm.as<float>(), h32, next_norm, true, eps, T,
+                                                    static_cast<int>(D), last ? fin : nullptr, last ? nullptr : x16,
+                                                    s));
+            }
+        }
+    }
+    {
+        Scope sc(e, CAT_OTHER, s);
+        FE_TRY_CUDA(fe::launch_pool_l2(fin, cu, batch, static_cast<int>(D), c.pooling, out, s));
+    }
+    return FE_OK;
+}
+
+bool config_rms_ok(const fe_rms_encoder_config *c, std::string &why)
+{
+    if (c->family != FE_FAMILY_QWEN3 && c->family != FE_FAMILY_GEMMA3) {
+        why = "family must be FE_FAMILY_QWEN3 or FE_FAMILY_GEMMA3";
+        return false;
+    }
+    if (c->vocab_size <= 0 || c->hidden <= 0 || c->layers <= 0 || c->q_heads <= 0 || c->kv_heads <= 0 ||
+        c->intermediate <= 0 || c->max_position <= 0) {
+        why = "all sizes must be positive";
+        return false;
+    }
+    if (c->head_dim != 128 && c->head_dim != 256) {
+        why = "head_dim must be 128 or 256";
+        return false;
+    }
+    if (c->q_heads % c->kv_heads != 0) {
+        why = "q_heads must be a multiple of kv_heads";
+        return false;
+    }
+    const int v = c->hidden / 128;
+    if (c->hidden % 128 != 0 || !(v == 2 || v == 3 || v == 4 || v == 6 || v == 8 || v == 12 || v == 16)) {
+        why = "hidden must be 256, 384, 512, 768, 1024, 1536 or 2048";
+        return false;
+    }
+    if (c->intermediate % 64 != 0) {
+        why = "intermediate must be a multiple of 64";
+        return false;
+    }
+    if (!(c->rope_theta > 1.0f) || (c->full_attention_every > 0 && !(c->rope_theta_local > 1.0f))) {
+        why = "rope_theta must be above 1";
+        return false;
+    }
+    if (c->pooling < FE_POOL_CLS || c->pooling > FE_POOL_LAST) {
+        why = "unknown pooling";
+        return false;
+    }
+    return true;
+}
+
 bool config_ok(const fe_encoder_config *c, std::string &why)
 {
     if (c->hidden <= 0 || c->layers <= 0 || c->heads <= 0 || c->intermediate <= 0 || c->vocab_size <= 0 ||
@@ -385,6 +639,37 @@ fe_status fe_engine_create(const fe_encoder_config *cfg, int device, fe_engine *
     return FE_OK;
 }
 
+fe_status fe_engine_create_rms(const fe_rms_encoder_config *cfg, int device, fe_engine **out)
+{
+    if (!cfg || !out) return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_create_rms: null argument");
+    *out = nullptr;
+    std::string why;
+    if (!config_rms_ok(cfg, why)) return fail(FE_ERR_UNSUPPORTED, "fe_engine_create_rms: " + why);
+    int n = 0;
+    FE_TRY_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_create_rms: bad device index");
+    cudaDeviceProp prop{};
+    FE_TRY_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(FE_ERR_UNSUPPORTED, "fe_engine_create_rms: this build targets sm_100a (B200)");
+    DeviceGuard g(device);
+    auto *e = new fe_engine();
+    e->family = cfg->family;
+    e->rc = *cfg;
+    e->device = device;
+    cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    if (err != cudaSuccess) {
+        delete e;
+        return fe::check_cuda(err, "cudaStreamCreate");
+    }
+    fe_status st = alloc_weights_rms(e);
+    if (st != FE_OK) {
+        fe_engine_destroy(e);
+        return st;
+    }
+    *out = e;
+    return FE_OK;
+}
+
 fe_status fe_engine_destroy(fe_engine *e)
 {
     if (!e) return FE_OK;
@@ -400,7 +685,9 @@ fe_status fe_engine_set_weight(fe_engine *e, const char *name, const float *data
 {
     if (!e || !name || (count && !data)) return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_set_weight: null argument");
     auto it = e->slots.find(name);
+    if (it == e->slots.end() && std::strncmp(name, "model.", 6) == 0) it = e->slots.find(name + 6);
     if (it == e->slots.end()) return fail(FE_ERR_NOT_FOUND, std::string("unknown tensor ") + name);
+    const std::string key = it->first;
     const Slot &sl = it->second;
     if (count != sl.count)
         return fail(FE_ERR_INVALID_ARGUMENT, std::string("tensor ") + name + ": expected " + std::to_string(sl.count) +
@@ -418,11 +705,21 @@ fe_status fe_engine_set_weight(fe_engine *e, const char *name, const float *data
             FE_TRY_CUDA(cudaMemcpyAsync(e->staging.p, data, count * sizeof(float), kind, e->stream));
             src = e->staging.as<float>();
         }
-        FE_TRY_CUDA(fe::launch_f32_to_bf16(src, static_cast<__nv_bfloat16 *>(sl.buf->p) + sl.offset,
-                                           static_cast<int64_t>(count), e->stream));
+        auto *dst = static_cast<__nv_bfloat16 *>(sl.buf->p) + sl.offset;
+        if (!sl.interleave) {
+            FE_TRY_CUDA(fe::launch_f32_to_bf16(src, dst, static_cast<int64_t>(count), e->stream));
+        } else {
+            // [F, row] into every other 32-row block of the [2F, row] gate-up matrix
+            FE_TRY_CUDA(e->staging16.ensure(count * sizeof(__nv_bfloat16)));
+            FE_TRY_CUDA(fe::launch_f32_to_bf16(src, e->staging16.as<__nv_bfloat16>(), static_cast<int64_t>(count),
+                                               e->stream));
+            const size_t block = 32 * sl.row * sizeof(__nv_bfloat16);
+            FE_TRY_CUDA(cudaMemcpy2DAsync(dst + (sl.interleave == 2 ? 32 * sl.row : 0), 2 * block, e->staging16.p,
+                                          block, block, count / (32 * sl.row), cudaMemcpyDeviceToDevice, e->stream));
+        }
     }
     FE_TRY_CUDA(cudaStreamSynchronize(e->stream));
-    e->loaded[name] = true;
+    e->loaded[key] = true;
     return FE_OK;
 }
 
@@ -509,6 +806,7 @@ fe_status fe_engine_encode_packed(fe_engine *e, const int32_t *ids, const int32_
     DeviceGuard g(e->device);
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : e->stream;
     if (batch == 0) return FE_OK;
+    if (e->family != FE_FAMILY_BERT) return forward_rms(e, ids, cu_seqlens, cu_seqlens_host, batch, out, s);
     return forward(e, ids, cu_seqlens, cu_seqlens_host, batch, out, s);
 }
 
@@ -529,7 +827,7 @@ fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t 
             return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_encode_host: length outside [0, stride]");
         T += lengths[b];
     }
-    const size_t D = e->cfg.hidden;
+    const size_t D = e->family == FE_FAMILY_BERT ? e->cfg.hidden : e->rc.hidden;
     FE_TRY_CUDA(e->p_ids.ensure(std::max<int64_t>(T, 1) * 4));
     FE_TRY_CUDA(e->p_cu.ensure((batch + 1) * 4));
     FE_TRY_CUDA(e->p_out.ensure(batch * D * 4));
@@ -540,8 +838,12 @@ fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t 
     cudaStream_t s = e->stream;
     FE_TRY_CUDA(cudaMemcpyAsync(e->d_ids.p, e->p_ids.p, T * 4, cudaMemcpyHostToDevice, s));
     FE_TRY_CUDA(cudaMemcpyAsync(e->d_cu.p, e->p_cu.p, (batch + 1) * 4, cudaMemcpyHostToDevice, s));
-    FE_TRY(forward(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), batch,
-                   e->d_out.as<float>(), s));
+    if (e->family != FE_FAMILY_BERT)
+        FE_TRY(forward_rms(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), batch,
+                           e->d_out.as<float>(), s));
+    else
+        FE_TRY(forward(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), batch,
+                       e->d_out.as<float>(), s));
     FE_TRY_CUDA(cudaMemcpyAsync(e->p_out.p, e->d_out.p, batch * D * 4, cudaMemcpyDeviceToHost, s));
     FE_TRY_CUDA(cudaStreamSynchronize(s));
     std::memcpy(out, e->p_out.p, batch * D * 4);

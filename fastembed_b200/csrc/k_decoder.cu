@@ -3,7 +3,7 @@
 // definitions: RMSNorm y = x / sqrt(mean(x^2) + eps) * w (Qwen3) or * (1 + w) (Gemma3),
 // computed in fp32; rotary embeddings in the rotate-half form with inverse frequencies
 // theta^(-2i/d), positions counted from 0 within each sentence.  One warp per row or per
-// (token, head); HBM-bound.
+// token; HBM-bound.
 #include <cuda_bf16.h>
 
 #include "fe_common.cuh"
@@ -135,27 +135,14 @@ __global__ void __launch_bounds__(256)
 }
 
 // Per-head RMSNorm and rotary embedding of the query and key heads, in place on the bf16
-// qkv buffer [T, (q_heads + 2 kv_heads) * HD].  One warp per (token, head); lane l holds
-// elements [E * l, E * (l + 1)), E = HD / 32, and its rotation partner (i +- HD/2) sits in
-// lane l ^ 16.
+// qkv buffer [T, (q_heads + 2 kv_heads) * HD].  One warp per token: the rotation angles
+// depend only on (position, frequency), so each lane computes the cos / sin of its E = HD/32
+// elements once and applies them to every query and key head of the token.  Lane l holds
+// elements [E * l, E * (l + 1)) of a head; its rotation partner (i +- HD/2) is in lane l ^ 16.
 template <int HD>
-__global__ void __launch_bounds__(256)
-    qk_norm_rope(__nv_bfloat16 *qkv, const int32_t *__restrict__ cu, int batch, int64_t total, int q_heads,
-                 int kv_heads, const float *__restrict__ q_w, const float *__restrict__ k_w, int one_plus, float eps,
-                 float log2_theta)
+__device__ __forceinline__ void load_head(const __nv_bfloat16 *p, float (&x)[HD / 32])
 {
-    constexpr int E = HD / 32;
-    const int nh = q_heads + kv_heads;
-    const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (gw >= total * nh) return;
-    const int64_t t = gw / nh;
-    const int h = static_cast<int>(gw % nh);
-    const int pos = static_cast<int>(t - cu[sentence_of(cu, batch, t)]);
-    __nv_bfloat16 *p = qkv + t * static_cast<int64_t>(q_heads + 2 * kv_heads) * HD + h * HD + E * lane;
-    const float *w = h < q_heads ? q_w : k_w;
-    float x[E];
-    if constexpr (E == 4) {
+    if constexpr (HD == 128) {
         const uint2 u = *reinterpret_cast<const uint2 *>(p);
         const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
         x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
@@ -164,31 +151,62 @@ __global__ void __launch_bounds__(256)
         const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
         x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y, x[4] = c.x, x[5] = c.y, x[6] = d.x, x[7] = d.y;
     }
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < E; ++i) s += x[i] * x[i];
-    const float r = rsqrtf(warp_sum(s) / static_cast<float>(HD) + eps);
-#pragma unroll
-    for (int i = 0; i < E; ++i) {
-        const float g = w[E * lane + i] + (one_plus ? 1.f : 0.f);
-        x[i] = x[i] * r * g;
-    }
-    const bool lo = lane < 16;  // elements i < HD/2
-    float y[E];
-#pragma unroll
-    for (int i = 0; i < E; ++i) {
-        const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
-        const int fi = (E * lane + i) & (HD / 2 - 1);  // frequency index
-        const float inv_freq = exp2f(-log2_theta * static_cast<float>(2 * fi) / static_cast<float>(HD));
-        float sn, cs;
-        sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
-        y[i] = lo ? x[i] * cs - partner * sn : x[i] * cs + partner * sn;
-    }
-    if constexpr (E == 4) {
+}
+
+template <int HD>
+__device__ __forceinline__ void store_head(__nv_bfloat16 *p, const float (&y)[HD / 32])
+{
+    if constexpr (HD == 128) {
         *reinterpret_cast<uint2 *>(p) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
     } else {
         *reinterpret_cast<uint4 *>(p) = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
                                                    pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+    }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256)
+    qk_norm_rope(__nv_bfloat16 *qkv, const int32_t *__restrict__ cu, int batch, int64_t total, int q_heads,
+                 int kv_heads, const float *__restrict__ q_w, const float *__restrict__ k_w, int one_plus, float eps,
+                 float log2_theta)
+{
+    constexpr int E = HD / 32;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= total) return;
+    const int pos = static_cast<int>(t - cu[sentence_of(cu, batch, t)]);
+    float cs[E], sn[E], wq[E], wk[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const int e = E * lane + i;
+        const int fi = e & (HD / 2 - 1);  // frequency index
+        const float inv_freq = exp2f(-log2_theta * static_cast<float>(2 * fi) / static_cast<float>(HD));
+        sincosf(static_cast<float>(pos) * inv_freq, &sn[i], &cs[i]);
+        wq[i] = q_w[e] + (one_plus ? 1.f : 0.f);
+        wk[i] = k_w[e] + (one_plus ? 1.f : 0.f);
+    }
+    const bool lo = lane < 16;  // elements i < HD/2
+    __nv_bfloat16 *row = qkv + t * static_cast<int64_t>(q_heads + 2 * kv_heads) * HD + E * lane;
+    const int nh = q_heads + kv_heads;
+#pragma unroll 2
+    for (int h = 0; h < nh; ++h) {
+        __nv_bfloat16 *p = row + h * HD;
+        float x[E];
+        load_head<HD>(p, x);
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) s += x[i] * x[i];
+        const float r = rsqrtf(warp_sum(s) / static_cast<float>(HD) + eps);
+        const bool is_q = h < q_heads;
+#pragma unroll
+        for (int i = 0; i < E; ++i) x[i] = x[i] * r * (is_q ? wq[i] : wk[i]);
+        float y[E];
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
+            y[i] = lo ? x[i] * cs[i] - partner * sn[i] : x[i] * cs[i] + partner * sn[i];
+        }
+        store_head<HD>(p, y);
     }
 }
 
@@ -242,7 +260,7 @@ cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t
                                 cudaStream_t s)
 {
     if (total == 0) return cudaSuccess;
-    const unsigned grid = grid_rows(total * (q_heads + kv_heads), 8);
+    const unsigned grid = grid_rows(total, 8);
     auto *p = static_cast<__nv_bfloat16 *>(qkv);
     const float lt = log2f(theta);
     if (head_dim == 128)

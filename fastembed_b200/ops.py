@@ -213,13 +213,22 @@ class Engine:
     """One device-resident encoder (fe_engine) on one GPU."""
 
     def __init__(self, shape, device: int = 0, pooling: str = "cls"):
+        """`shape`: a workload.EncoderShape (post-LN BERT) or workload.RmsShape (Qwen3 /
+        Gemma3 shapes, whose pooling comes with the family)."""
         self.shape = shape
         self.device = device
-        cfg = capi.EncoderConfig(shape.vocab, shape.hidden, shape.layers, shape.heads, shape.intermediate,
-                                 shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], POOL[pooling])
-        self._cfg = cfg
         h = C.c_void_p()
-        capi.check(capi.lib().fe_engine_create(C.byref(cfg), device, C.byref(h)), "fe_engine_create")
+        if hasattr(shape, "family"):
+            cfg = capi.RmsEncoderConfig(capi.FAMILY[shape.family], shape.vocab, shape.hidden, shape.layers,
+                                        shape.q_heads, shape.kv_heads, shape.head_dim, shape.intermediate,
+                                        shape.max_pos, shape.eps, shape.rope_theta, shape.rope_theta_local,
+                                        shape.full_every, 0.0, POOL[shape.pooling])
+            capi.check(capi.lib().fe_engine_create_rms(C.byref(cfg), device, C.byref(h)), "fe_engine_create_rms")
+        else:
+            cfg = capi.EncoderConfig(shape.vocab, shape.hidden, shape.layers, shape.heads, shape.intermediate,
+                                     shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], POOL[pooling])
+            capi.check(capi.lib().fe_engine_create(C.byref(cfg), device, C.byref(h)), "fe_engine_create")
+        self._cfg = cfg
         self.h = h
 
     def close(self):

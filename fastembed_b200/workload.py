@@ -196,3 +196,144 @@ def balanced_cuts(shape: EncoderShape, sorted_lengths: np.ndarray, parts: int) -
         lo = cuts[-1] if cuts else 0
         cuts.append(int(min(max(i, lo), sorted_lengths.size)))
     return cuts
+
+
+# ------------------------------------------------ pre-RMSNorm rotary encoders
+@dataclasses.dataclass(frozen=True)
+class RmsShape:
+    """Qwen3 / Gemma3-shaped encoder (not in the reference; built from the model
+    definitions).  `family` is "qwen3" (causal, SwiGLU, w norms, last-token pooling) or
+    "gemma3" (bidirectional, GeGLU, (1 + w) norms, sandwich norms, mean pooling)."""
+    name: str
+    family: str
+    layers: int
+    hidden: int
+    q_heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    max_pos: int = 32768
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+    rope_theta_local: float = 1e4
+    full_every: int = 0
+    batch: int = 8
+    lengths: tuple = ("uniform", 16, 128)
+
+    @property
+    def pooling(self) -> str:
+        return "last" if self.family == "qwen3" else "mean"
+
+    @property
+    def causal(self) -> bool:
+        return self.family == "qwen3"
+
+    def _qkv(self) -> int:
+        return (self.q_heads + 2 * self.kv_heads) * self.head_dim
+
+    def gemm_flops_per_sentence(self, length: int) -> float:
+        D, F, L, AO = self.hidden, self.intermediate, length, self.q_heads * self.head_dim
+        return self.layers * 2.0 * L * (D * self._qkv() + AO * D + 3 * D * F)
+
+    def attn_flops_per_sentence(self, length: int) -> float:
+        pairs = length * (length + 1) / 2 if self.causal else length * length
+        return self.layers * 4.0 * pairs * self.q_heads * self.head_dim
+
+    def flops_per_sentence(self, length: int) -> float:
+        return self.gemm_flops_per_sentence(length) + self.attn_flops_per_sentence(length)
+
+
+RMS_SHAPES = {
+    # Qwen3-0.6B shape: 28 layers, D 1024, 16 q / 8 kv heads x 128, FFN 3072 SwiGLU, causal;
+    # batch 128, L ~ U[64, 1024]
+    "qwen3-0.6b": RmsShape("qwen3-0.6b", "qwen3", 28, 1024, 16, 8, 128, 3072, 151936, batch=128,
+                           lengths=("uniform", 64, 1024)),
+    # Gemma-300M (EmbeddingGemma) shape: 24 layers, D 768, 3 q / 1 kv heads x 256, FFN 1152
+    # GeGLU, bidirectional, every 6th layer global; batch 512, L ~ U[8, 256]
+    "gemma-300m": RmsShape("gemma-300m", "gemma3", 24, 768, 3, 1, 256, 1152, 262144, max_pos=2048,
+                           rope_theta=1e6, rope_theta_local=1e4, full_every=6, batch=512,
+                           lengths=("uniform", 8, 256)),
+    # two-layer test shapes
+    "qwen3-tiny": RmsShape("qwen3-tiny", "qwen3", 2, 256, 4, 2, 128, 384, 1000, batch=6,
+                           lengths=("uniform", 1, 300)),
+    "gemma3-tiny": RmsShape("gemma3-tiny", "gemma3", 2, 768, 3, 1, 256, 1152, 1000, max_pos=2048, full_every=2,
+                            batch=6, lengths=("uniform", 1, 300)),
+}
+
+
+def rms_weight_names(shape: RmsShape) -> list[tuple[str, tuple[int, ...], str]]:
+    """(HF name, shape, init) of every tensor of the Qwen3Model / Gemma3TextModel layout.
+    Norm weights: Qwen3 multiplies by w (init 1), Gemma3 by (1 + w) (init 0)."""
+    D, F, hd = shape.hidden, shape.intermediate, shape.head_dim
+    one = "zeros" if shape.family == "gemma3" else "ones"
+    out = [("embed_tokens.weight", (shape.vocab, D), "normal")]
+    for l in range(shape.layers):
+        p = f"layers.{l}."
+        out += [
+            (p + "self_attn.q_proj.weight", (shape.q_heads * hd, D), "normal"),
+            (p + "self_attn.k_proj.weight", (shape.kv_heads * hd, D), "normal"),
+            (p + "self_attn.v_proj.weight", (shape.kv_heads * hd, D), "normal"),
+            (p + "self_attn.o_proj.weight", (D, shape.q_heads * hd), "normal"),
+            (p + "self_attn.q_norm.weight", (hd,), one),
+            (p + "self_attn.k_norm.weight", (hd,), one),
+            (p + "mlp.gate_proj.weight", (F, D), "normal"),
+            (p + "mlp.up_proj.weight", (F, D), "normal"),
+            (p + "mlp.down_proj.weight", (D, F), "normal"),
+            (p + "input_layernorm.weight", (D,), one),
+            (p + "post_attention_layernorm.weight", (D,), one),
+        ]
+        if shape.family == "gemma3":
+            out += [(p + "pre_feedforward_layernorm.weight", (D,), one),
+                    (p + "post_feedforward_layernorm.weight", (D,), one)]
+    out += [("norm.weight", (D,), one)]
+    return out
+
+
+def make_rms_weights(shape: RmsShape, seed: int = 0, std: float = 0.02,
+                     norm_jitter: float = 0.0) -> dict[str, np.ndarray]:
+    """Seeded random-init FP32 weights keyed by HF name; `norm_jitter` adds N(0, jitter)
+    to the norm weights (tests use it so that the weight form matters)."""
+    rng = np.random.default_rng(seed)
+    w: dict[str, np.ndarray] = {}
+    for name, shp, init in rms_weight_names(shape):
+        if init == "normal":
+            a = rng.standard_normal(size=shp, dtype=np.float32) * np.float32(std)
+        else:
+            a = np.ones(shp, dtype=np.float32) if init == "ones" else np.zeros(shp, dtype=np.float32)
+            if norm_jitter:
+                a = a + rng.standard_normal(size=shp, dtype=np.float32) * np.float32(norm_jitter)
+        w[name] = a
+    return w
+
+
+def rms_hf_config(shape: RmsShape) -> dict:
+    """transformers config keyword arguments of the same model (used by the oracle)."""
+    common = dict(vocab_size=shape.vocab, hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                  num_hidden_layers=shape.layers, num_attention_heads=shape.q_heads,
+                  num_key_value_heads=shape.kv_heads, head_dim=shape.head_dim,
+                  max_position_embeddings=shape.max_pos, rms_norm_eps=shape.eps, attention_bias=False)
+    if shape.family == "qwen3":
+        return dict(common, rope_theta=shape.rope_theta, hidden_act="silu", tie_word_embeddings=False)
+    types = ["full_attention" if shape.full_every and (l + 1) % shape.full_every == 0 else "sliding_attention"
+             for l in range(shape.layers)]
+    return dict(common, hidden_activation="gelu_pytorch_tanh", use_bidirectional_attention=True,
+                query_pre_attn_scalar=shape.head_dim, layer_types=types, sliding_window=2 * shape.max_pos + 1,
+                rope_parameters={"full_attention": {"rope_type": "default", "rope_theta": shape.rope_theta},
+                                 "sliding_attention": {"rope_type": "default", "rope_theta": shape.rope_theta_local}})
+
+
+def sample_rms_lengths(shape: RmsShape, batch: int | None = None, seed: int = 1) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    _, lo, hi = shape.lengths
+    return rng.integers(lo, hi + 1, size=batch or shape.batch).astype(np.int32)
+
+
+def sample_rms_ids(shape: RmsShape, lengths: np.ndarray, seed: int = 1) -> np.ndarray:
+    """Right-padded ids [B, max L] uniform in [100, vocab) (no framing tokens)."""
+    rng = np.random.default_rng(seed + 1000)
+    S = max(int(lengths.max()) if lengths.size else 1, 1)
+    ids = np.zeros((lengths.size, S), dtype=np.int32)
+    for b, L in enumerate(lengths):
+        ids[b, :int(L)] = rng.integers(100, shape.vocab, size=int(L))
+    return ids

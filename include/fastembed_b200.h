@@ -227,6 +227,33 @@ typedef struct fe_encoder_config {
     int32_t pooling;    /* fe_pooling */
 } fe_encoder_config;
 
+/* Pre-RMSNorm rotary encoders, the Qwen3 and Gemma3 shapes (not in the reference; the
+ * forward follows the model definitions):
+ *   FE_FAMILY_QWEN3   x <- x + Wo attn(rope(qknorm(Wqkv rms(x))), causal);
+ *                     x <- x + Wd (silu(Wg rms(x)) * Wu rms(x)); final RMSNorm; w weights
+ *   FE_FAMILY_GEMMA3  embeddings scaled by sqrt(hidden);
+ *                     x <- x + rms(Wo attn(rope(qknorm(Wqkv rms(x)))), bidirectional);
+ *                     x <- x + rms(Wd (gelu_tanh(Wg rms(x)) * Wu rms(x))); final RMSNorm;
+ *                     (1 + w) weights; layers l with (l + 1) % full_attention_every == 0 use
+ *                     rope_theta, the others rope_theta_local.
+ * Weights by HF name (embed_tokens.weight, layers.N.self_attn.{q,k,v,o}_proj.weight,
+ * layers.N.self_attn.{q,k}_norm.weight, layers.N.mlp.{gate,up,down}_proj.weight,
+ * layers.N.{input,post_attention}_layernorm.weight, Gemma3 also
+ * layers.N.{pre,post}_feedforward_layernorm.weight, norm.weight), with or without a
+ * leading "model.". */
+typedef enum fe_family { FE_FAMILY_BERT = 0, FE_FAMILY_QWEN3 = 1, FE_FAMILY_GEMMA3 = 2 } fe_family;
+
+typedef struct fe_rms_encoder_config {
+    int32_t family; /* FE_FAMILY_QWEN3 or FE_FAMILY_GEMMA3 */
+    int32_t vocab_size, hidden, layers, q_heads, kv_heads, head_dim, intermediate, max_position;
+    float rms_norm_eps;
+    float rope_theta;             /* global-attention layers */
+    float rope_theta_local;       /* sliding-window layers (Gemma3) */
+    int32_t full_attention_every; /* Gemma3 layer pattern; 0: every layer uses rope_theta */
+    float query_scale;            /* attention scale; 0: head_dim^-0.5 */
+    int32_t pooling;              /* fe_pooling: FE_POOL_LAST (Qwen3), FE_POOL_MEAN (Gemma3) */
+} fe_rms_encoder_config;
+
 typedef struct fe_engine fe_engine;
 
 typedef struct fe_engine_stats {
@@ -244,6 +271,11 @@ typedef struct fe_engine_stats {
  * SentenceTransformerImpl constructor (src/sentence_transformers_impl.cpp:46-98). */
 fe_status fe_engine_create(const fe_encoder_config *cfg, int device, fe_engine **out);
 fe_status fe_engine_destroy(fe_engine *e);
+/* Creates an engine for a pre-RMSNorm rotary encoder (Qwen3 / Gemma3 shapes).  Requires
+ * head_dim 128 or 256, q_heads % kv_heads == 0, hidden in {256, 384, 512, 768, 1024, 1536,
+ * 2048}, intermediate % 64 == 0; Gemma3 sentences up to 1024 tokens. */
+fe_status fe_engine_create_rms(const fe_rms_encoder_config *cfg, int device, fe_engine **out);
+
 /* Uploads one FP32 tensor by its HF name (the keys of the reference's weights map,
  * src/sentence_transformers_impl.cpp:201-218).  `data` is host memory unless
  * data_on_device != 0.  Unknown names return FE_ERR_NOT_FOUND; a wrong element
