@@ -77,6 +77,7 @@ _SIGS = {
     "fe_layernorm_dual": ([vp, vp, vp, vp, vp, vp, i64, i32, f32, vp], C.c_int),
     "fe_attention_varlen_gqa_bf16": ([vp, vp, i32, i32, i32, i32, i32, i32, f32, vp, i64, vp], C.c_int),
     "fe_linear_layernorm_workspace_bytes": ([i64, i64, C.POINTER(sz)], C.c_int),
+    "fe_linear_rmsnorm_bf16": ([vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, vp, sz, vp], C.c_int),
     "fe_linear_layernorm_bf16": ([vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, vp, sz, vp], C.c_int),
     "fe_embed_scale": ([vp, i64, vp, i32, i32, f32, vp, vp], C.c_int),
     "fe_rms_norm_rows": ([vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),

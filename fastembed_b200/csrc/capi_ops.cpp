@@ -273,6 +273,33 @@ fe_status fe_linear_layernorm_bf16(const void *x, const void *w, const float *bi
     return done(e, "fe_linear_layernorm_bf16");
 }
 
+fe_status fe_linear_rmsnorm_bf16(const void *x, const void *w, const float *bias, const float *rms_w, float *h32,
+                                 void *h16, int64_t m, int64_t n, int64_t k, float eps, void *workspace,
+                                 size_t workspace_bytes, fe_stream_t stream)
+{
+    if (m < 0 || n <= 0 || k <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_bf16: bad shape");
+    if (k % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_bf16: k must be a multiple of 8");
+    if (n > 0x7fffffff || !supported_row_dim(static_cast<int32_t>(n)) || n == 128)
+        return fail(FE_ERR_UNSUPPORTED, "fe_linear_rmsnorm_bf16: n must be 256, 384, 512, 768, 1024, 1536 or 2048");
+    if (m > 0x7fffffff || k > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_linear_rmsnorm_bf16: size too large");
+    if (m == 0) return FE_OK;
+    if (!x || !w || !bias || !rms_w || !h32 || !workspace)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_bf16: null pointer");
+    if (workspace_bytes < fe::linear_layernorm_workspace_bytes(m, n))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_bf16: workspace too small");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(bias) || !aligned16(rms_w) || !aligned16(h32) ||
+        (h16 && !aligned16(h16)) || !aligned16(workspace))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_bf16: pointers must be 16-byte aligned");
+    void *stats = nullptr;
+    float *y = nullptr;
+    fe::linear_layernorm_split_workspace(workspace, m, n, &stats, &y);
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_linear_layernorm(x, w, bias, rms_w, nullptr, h32, h16, m, n, k, eps, stats, y,
+                                                reinterpret_cast<cudaStream_t>(stream), &st, true);
+    if (st != FE_OK) return st;
+    return done(e, "fe_linear_rmsnorm_bf16");
+}
+
 static bool rms_dim_ok(int32_t dim) { return supported_row_dim(dim) && dim != 128; }
 
 fe_status fe_embed_scale(const int32_t *ids, int64_t total_tokens, const float *word, int32_t vocab, int32_t dim,

@@ -395,6 +395,9 @@ fe_status ensure_activations_rms(fe_engine *e, int64_t T)
     FE_TRY_CUDA(e->y32.ensure(cap * D * 4));
     FE_TRY_CUDA(e->ff.ensure(cap * F * 2));
     FE_TRY_CUDA(e->hfin.ensure(cap * D * 4));
+    const size_t ws = fe::linear_layernorm_stats_bytes(cap, static_cast<int64_t>(D));
+    FE_TRY_CUDA(e->ln_ws.ensure(ws));
+    FE_TRY_CUDA(cudaMemset(e->ln_ws.p, 0, ws));
     e->cap_tokens = cap;
     return FE_OK;
 }
@@ -454,6 +457,16 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
         if (st != FE_OK) return st;
         return fe::check_cuda(err, "linear");
     };
+    // pre-norm projection + residual + RMSNorm: fused where the launcher can (long K), else two launches
+    auto linear_rms = [&](const void *x, const DevBuf &w, const DevBuf &norm_w, float *h, void *out16, int64_t n,
+                          int64_t k) -> fe_status {
+        Scope sc(e, CAT_GEMM, s);
+        fe_status st = FE_OK;
+        cudaError_t err = fe::launch_linear_layernorm(x, w.p, e->zero_bias.as<float>(), norm_w.as<float>(), nullptr, h,
+                                                      out16, T, n, k, eps, e->ln_ws.p, nullptr, s, &st, true);
+        if (st != FE_OK) return st;
+        return fe::check_cuda(err, "linear+RMSNorm");
+    };
     {
         Scope sc(e, CAT_OTHER, s);
         // Gemma3 scales the embeddings by sqrt(hidden) (rounded to fp32); Qwen3 does not
@@ -486,19 +499,16 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
         }
         const float *next_norm = last ? e->final_norm.as<float>() : e->rlayers[l + 1].in_norm.as<float>();
         if (!gemma) {
-            // x <- x + attn Wo^T (residual in the GEMM epilogue, in place); then the post-attention norm
-            FE_TRY(gemm(attn, L.wo, e->zero_bias.as<float>(), h32, h32, D, AO, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32));
-            {
-                Scope sc(e, CAT_OTHER, s);
-                FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, L.post_attn_norm.as<float>(), false, eps, T,
-                                                     static_cast<int>(D), nullptr, x16, s));
-            }
+            // x <- x + attn Wo^T and the post-attention RMSNorm into x16, one fused step
+            FE_TRY(linear_rms(attn, L.wo, L.post_attn_norm, h32, x16, D, AO));
             FE_TRY(gemm(x16, L.wgu, nullptr, nullptr, ff, 2 * F, D, FE_EPI_SWIGLU, FE_DTYPE_BF16));
-            FE_TRY(gemm(ff, L.wd, e->zero_bias.as<float>(), h32, h32, D, F, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32));
-            {
+            // x <- x + ff Wd^T and the next layer's input RMSNorm (the final norm: below, in fp32)
+            FE_TRY(linear_rms(ff, L.wd, last ? e->final_norm : e->rlayers[l + 1].in_norm, h32, last ? nullptr : x16, D,
+                              F));
+            if (last) {
                 Scope sc(e, CAT_OTHER, s);
-                FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, next_norm, false, eps, T, static_cast<int>(D),
-                                                     last ? fin : nullptr, last ? nullptr : x16, s));
+                FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, next_norm, false, eps, T, static_cast<int>(D), fin, nullptr,
+                                                     s));
             }
         } else {
             // x <- x + rms(attn Wo^T), then the pre-FFN norm, in one row kernel

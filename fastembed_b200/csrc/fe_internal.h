@@ -62,9 +62,11 @@ cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
 size_t linear_layernorm_workspace_bytes(int64_t m, int64_t n);
 size_t linear_layernorm_stats_bytes(int64_t m, int64_t n);  // the statistics head of it
 void linear_layernorm_split_workspace(void *ws, int64_t m, int64_t n, void **stats, float **y);
+// rms: pre-norm RMSNorm form instead: h32 <- (x W^T + bias) + h32, h16 <- RMSNorm(h32) * gamma.
 cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *bias, const float *gamma,
                                     const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
-                                    float eps, void *stats, float *y_fallback, cudaStream_t s, fe_status *st);
+                                    float eps, void *stats, float *y_fallback, cudaStream_t s, fe_status *st,
+                                    bool rms = false);
 // qkv / out layouts: token-major [T, 3*H*64] / [T, H*64], or head-major
 // [3*H, T, 64] / [H, T, 64] when head_major is true.
 cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, int batch,

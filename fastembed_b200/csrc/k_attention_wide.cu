@@ -14,9 +14,9 @@
 //              O (+)= P V with P (bf16) read from TMEM and V an MN-major operand; the
 //              first item of a unit overwrites O.
 //   warps 2-5  softmax (thread = query row): masked online softmax over S, P written back
-//              over S; when a row's running max rises, O is rescaled in TMEM after the
-//              previous item's PV and before this one's; after a unit's last PV, O / l
-//              is stored as bf16.
+//              over S; when a row's reference max rises (by more than 2^8 in P), O is
+//              rescaled in TMEM after the previous item's PV and before this one's; after a
+//              unit's last PV, O / l is stored as bf16.
 // Waits are bounded; on timeout the CTA records FE_ERR_DEVICE_TIMEOUT and leaves.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -331,10 +331,13 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                         for (int i = 0; i < 32; ++i)
                             if (c + i < lim) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
                     }
-                    const float tmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-                    mx = fmaxf(m_run, tmax * scale_log2);
-                    // a row with no kept key yet (causal, past the diagonal) keeps m = -inf
-                    alpha = mx == -INFINITY ? 1.f : fast_exp2w(m_run - mx);
+                    const float tmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale_log2;
+                    // Lazy reference max: P = exp2(s - m) with m raised only when a tile's max
+                    // exceeds it by more than 8 (P <= 2^8 stays exact enough in fp32 sums and
+                    // bf16 P), so O in TMEM is rescaled only then.  O and l share the scale.
+                    if (m_run == -INFINITY || tmax > m_run + 8.0f) mx = fmaxf(m_run, tmax);
+                    // a row with no kept key yet keeps m = -inf
+                    alpha = mx == m_run ? 1.f : (m_run == -INFINITY ? 0.f : fast_exp2w(m_run - mx));
                     const float msub = mx == -INFINITY ? 0.f : mx;
                     for (int c = 0; c < valid; c += 32) {
                         uint32_t v[32];

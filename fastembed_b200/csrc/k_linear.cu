@@ -647,7 +647,6 @@ struct LnCfg {
     static_assert(SLABS == 1 || SLABS == 2, "fp32 slabs");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
-using LnLongK = LnCfg<6, 4, 1>;
 
 struct LnParams {
     const float *bias;
@@ -658,6 +657,8 @@ struct LnParams {
     unsigned epoch;             // nonzero, unique per launch on this workspace
     float eps;
     int nparts;                 // statistics partials per row = N / COLS
+    int rms;                    // 0: LayerNorm, h32 <- the normalised rows (post-norm);
+                                // 1: RMSNorm, h32 <- x itself, h16 <- x / rms(x) * gamma (pre-norm)
 };
 
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v)
@@ -928,7 +929,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
                 gm = pk + ps1 * inv_p;
                 gq = pq_sum + static_cast<float>(COLS) * fmaxf(ps2 - ps1 * ps1 * inv_p, 0.f);
             }
-            const float inv_sd = 1.0f / sqrtf(gq * inv_n + p.eps);
+            // LayerNorm: 1 / sqrt(var + eps); RMSNorm: 1 / sqrt(mean(x^2) + eps), mean(x^2) = var + mean^2
+            const float inv_sd = 1.0f / sqrtf(gq * inv_n + (p.rms ? gm * gm : 0.f) + p.eps);
 
             // ---- pass 2: normalise from TMEM, TMA-store fp32 and bf16.  Bulk groups per
             // chunk c: F(c) (fp32 slab c % SLABS), then B(c) (the bf16 slab).
@@ -940,24 +942,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
                 tmem_wait_ld_regs(cur);
                 if (c + 1 < CH) tmem_ld_x32(t_row + (c + 1) * 32, v[(c + 1) & 1]);
                 float o[32];
+                const float sub = p.rms ? 0.f : gm;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const float4 g = *reinterpret_cast<const float4 *>(vg + c * 32 + 4 * j);
-                    const float4 e = *reinterpret_cast<const float4 *>(ve + c * 32 + 4 * j);
-                    o[4 * j + 0] = (__uint_as_float(cur[4 * j + 0]) - gm) * inv_sd * g.x + e.x;
-                    o[4 * j + 1] = (__uint_as_float(cur[4 * j + 1]) - gm) * inv_sd * g.y + e.y;
-                    o[4 * j + 2] = (__uint_as_float(cur[4 * j + 2]) - gm) * inv_sd * g.z + e.z;
-                    o[4 * j + 3] = (__uint_as_float(cur[4 * j + 3]) - gm) * inv_sd * g.w + e.w;
+                    float4 e = *reinterpret_cast<const float4 *>(ve + c * 32 + 4 * j);
+                    if (p.rms) e = make_float4(0.f, 0.f, 0.f, 0.f);
+                    o[4 * j + 0] = (__uint_as_float(cur[4 * j + 0]) - sub) * inv_sd * g.x + e.x;
+                    o[4 * j + 1] = (__uint_as_float(cur[4 * j + 1]) - sub) * inv_sd * g.y + e.y;
+                    o[4 * j + 2] = (__uint_as_float(cur[4 * j + 2]) - sub) * inv_sd * g.z + e.z;
+                    o[4 * j + 3] = (__uint_as_float(cur[4 * j + 3]) - sub) * inv_sd * g.w + e.w;
                 }
                 // F(c - SLABS) has read slab b: at most 2 * SLABS - 1 newer groups pending
                 if (lane == 0) bulk_wait_read<2 * SLABS - 1>();
                 __syncwarp();
                 uint8_t *fs = wb + b * 4096;
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+                for (int j = 0; j < 8; ++j)  // 128B swizzle; pre-norm keeps x itself in the fp32 stream
                     *reinterpret_cast<uint4 *>(fs + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-                        make_uint4(__float_as_uint(o[4 * j + 0]), __float_as_uint(o[4 * j + 1]),
-                                   __float_as_uint(o[4 * j + 2]), __float_as_uint(o[4 * j + 3]));  // 128B swizzle
+                        p.rms ? make_uint4(cur[4 * j + 0], cur[4 * j + 1], cur[4 * j + 2], cur[4 * j + 3])
+                              : make_uint4(__float_as_uint(o[4 * j + 0]), __float_as_uint(o[4 * j + 1]),
+                                           __float_as_uint(o[4 * j + 2]), __float_as_uint(o[4 * j + 3]));
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -1090,6 +1095,14 @@ bool pair_mode_enabled()
     return !(v && v[0] == '0');
 }
 
+// FE_LINEAR_NORM_FUSE=0 takes the two-launch form of linear + residual + norm for every
+// shape (same result; used to compare the two forms on a workload).
+bool norm_fuse_enabled()
+{
+    const char *v = getenv("FE_LINEAR_NORM_FUSE");
+    return !(v && v[0] == '0');
+}
+
 }  // namespace
 
 cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
@@ -1172,22 +1185,55 @@ void linear_layernorm_split_workspace(void *ws, int64_t m, int64_t n, void **sta
     *y = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + linear_layernorm_stats_bytes(m, n));
 }
 
+namespace {
+using LnKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, int, int, int,
+                          LnParams, int, int *);
+struct LnVariant {
+    int (*resident)();
+    int cols, threads;
+    uint32_t smem;
+    LnKernel kern;
+};
+template <int S, int E, int L>
+LnVariant ln_variant()
+{
+    using Cf = LnCfg<S, E, L>;
+    return {&ln_resident_pairs<Cf, S, E, L>, Cf::COLS, Cf::THREADS, Cf::SMEM, &linear_ln_tcgen05_pair<S, E, L>};
+}
+// Ring depth against residual double-buffering (shared memory holds one or the other):
+// measured per launch at n = 1024 on one B200,
+//   k = 4096, m = 26508 (LayerNorm):  6 stages / 1 slab 216 us, 5 stages / 2 slabs 221 us;
+//   k = 3072, m = 71550 (RMSNorm):    468 us and 427 us;  k = 2048: 378 us and 344 us.
+// Eight epilogue warps were slower in every case (252-545 us).
+LnVariant pick_ln_variant(int64_t k)
+{
+    return k >= 4096 ? ln_variant<6, 4, 1>() : ln_variant<5, 4, 2>();
+}
+}  // namespace
+
 cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *bias, const float *gamma,
                                     const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
-                                    float eps, void *stats, float *y_fallback, cudaStream_t s, fe_status *st)
+                                    float eps, void *stats, float *y_fallback, cudaStream_t s, fe_status *st, bool rms)
 {
     *st = FE_OK;
     if (m == 0 || n == 0) return cudaSuccess;
     const int n_tiles = static_cast<int>(n / P_BN);
     // fused only where the mainloop hides the statistics exchange (see linear_ln_tcgen05_pair)
-    bool fused = k >= 2048 && pair_mode_enabled() && n % P_BN == 0 && n_tiles <= kMaxLnParts && stats;
+    bool fused = k >= 2048 && pair_mode_enabled() && norm_fuse_enabled() && n % P_BN == 0 && n_tiles <= kMaxLnParts && stats;
     int pairs = 0;
+    const LnVariant var = pick_ln_variant(k);
     if (fused) {
         const int tiles = static_cast<int>((m + 255) / 256) * n_tiles;
-        pairs = std::min(ln_resident_pairs<LnLongK, 6, 4, 1>(), current_sm_count() / 2);
+        pairs = std::min(var.resident(), current_sm_count() / 2);
         pairs = pairs / n_tiles * n_tiles;  // each row group's tiles in the same round
         if (pairs > tiles) pairs = tiles;
         fused = pairs >= n_tiles;
+    }
+    if (!fused && rms) {
+        // Unfused pre-norm form: x = x W^T + b + h32 in place, then RMSNorm into h16.
+        cudaError_t e = launch_linear_bf16(x, w, bias, h32, h32, m, n, k, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32, s, st);
+        if (e != cudaSuccess || *st != FE_OK || !h16) return e;
+        return launch_rms_norm_rows(h32, gamma, false, eps, m, static_cast<int>(n), nullptr, h16, s);
     }
     if (!fused) {
         // Unfused form of the same step: linear with bias into fp32, then residual + LayerNorm.
@@ -1214,10 +1260,11 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
     LnParams p;
     p.bias = bias;
     p.gamma = gamma;
-    p.beta = beta;
+    p.beta = beta ? beta : gamma;  // read into shared memory; unused by the RMSNorm form
     p.stats = static_cast<unsigned long long *>(stats);
     p.eps = eps;
-    p.nparts = static_cast<int>(n / LnLongK::COLS);
+    p.nparts = static_cast<int>(n / var.cols);
+    p.rms = rms ? 1 : 0;
     int dev = 0;
     cudaGetDevice(&dev);
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -1234,8 +1281,7 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
     const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
     const int w16 = h16 != nullptr;
     int *status = current_device_status_word();
-    linear_ln_tcgen05_pair<6, 4, 1><<<2 * pairs, LnLongK::THREADS, LnLongK::SMEM, s>>>(tx, tw, th, th16, M, N, K, p,
-                                                                                        w16, status);
+    var.kern<<<2 * pairs, var.threads, var.smem, s>>>(tx, tw, th, th16, M, N, K, p, w16, status);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (order) {

@@ -159,6 +159,19 @@ def linear_layernorm(x, w, bias, gamma, beta, h32, eps, workspace=None, want_h16
     return h32, h16
 
 
+def linear_rmsnorm(x, w, bias, rms_w, h32, eps, workspace=None, want_h16=True):
+    """Pre-norm: h32 <- (x @ w.T + bias) + h32 in place; returns (h32, bf16 RMSNorm(h32) * rms_w)."""
+    _cuda(x, w, bias, rms_w, h32)
+    m, k = x.shape
+    n = w.shape[0]
+    if workspace is None:
+        workspace = linear_layernorm_workspace(m, n, x.device)
+    h16 = torch.empty(m, n, dtype=torch.bfloat16, device=x.device) if want_h16 else None
+    call("fe_linear_rmsnorm_bf16", _p(x), _p(w), _p(bias), _p(rms_w), _p(h32), _p(h16), m, n, k, eps, _p(workspace),
+         workspace.numel(), _s(x))
+    return h32, h16
+
+
 def embed_scale(ids, word, scale):
     _cuda(ids, word)
     T = ids.numel()

@@ -190,6 +190,13 @@ fe_status fe_layernorm_dual(const float *x, const float *residual, const float *
  * must be zero-filled before its first use; it then serves any number of calls, with
  * any m up to the one it was sized for.  Calls that share a workspace must not run
  * concurrently. */
+/* Pre-norm RMSNorm form of the same step (Qwen3-shaped encoders; not in the reference):
+ *     h32 <- (x[m,k] · w[n,k]^T + bias) + h32      (in place: the residual stream)
+ *     h16 <- bf16(h32 / sqrt(mean(h32^2) + eps) * rms_w)   (the next layer input; may be NULL)
+ * bias is required (zeros for models without one).  Workspace as above. */
+fe_status fe_linear_rmsnorm_bf16(const void *x, const void *w, const float *bias, const float *rms_w, float *h32,
+                                 void *h16, int64_t m, int64_t n, int64_t k, float eps, void *workspace,
+                                 size_t workspace_bytes, fe_stream_t stream);
 fe_status fe_linear_layernorm_workspace_bytes(int64_t m, int64_t n, size_t *bytes);
 fe_status fe_linear_layernorm_bf16(const void *x, const void *w, const float *bias, const float *gamma,
                                    const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,

@@ -317,6 +317,33 @@ def test_linear_layernorm_rejects(cuda_dev):
         ops.linear_layernorm(x, w, b, gam, bet, res, 1e-12, workspace=small)
 
 
+# (m, n, k): Qwen3-0.6B's o_proj and down_proj (one launch), a single column tile, and the
+# two-launch form for k < 2048
+LINEAR_RMS_SHAPES = [(700, 1024, 2048), (1500, 1024, 3072), (130, 256, 2048), (333, 1024, 1024)]
+
+
+@pytest.mark.parametrize("pair", ["1", "0"])
+@pytest.mark.parametrize("m,n,k", LINEAR_RMS_SHAPES)
+def test_linear_rmsnorm(cuda_dev, monkeypatch, m, n, k, pair):
+    """Pre-norm: h32 <- (x W^T + b) + h32 stays un-normalised, h16 <- bf16(RMSNorm(h32) * w)."""
+    from fastembed_b200 import ops
+    monkeypatch.setenv("FE_LINEAR_PAIR", pair)
+    x, w, b, res, gam, _ = _linear_ln_inputs(m, n, k, 3 * m + n + k, cuda_dev)
+    y = (x.float() @ w.float().T + b) + res
+    ref16 = _rms_ref(y, gam, 1e-6, False)
+    ws = ops.linear_layernorm_workspace(m, n, cuda_dev)
+    for _ in range(2):  # the second call reuses the workspace (epoch-tagged statistics)
+        h32, h16 = ops.linear_rmsnorm(x, w, b, gam, res.clone(), 1e-6, workspace=ws)
+        torch.cuda.synchronize()
+        assert float((h32 - y).abs().max()) < 1e-3
+        err = (h16.float() - ref16).abs()
+        assert bool((err <= ref16.abs() * 2.0 ** -7 + 1e-4).all()), float(err.max())
+    h32n, none16 = ops.linear_rmsnorm(x, w, b, gam, res.clone(), 1e-6, workspace=ws, want_h16=False)
+    assert none16 is None
+    assert torch.equal(h32n, h32)
+    ops.device_status(0)
+
+
 @pytest.mark.parametrize("mode", ["cls", "mean", "last"])
 def test_pool_l2_indices(cuda_dev, mode):
     from fastembed_b200 import ops
