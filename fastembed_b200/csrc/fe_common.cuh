@@ -95,6 +95,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
+// Non-blocking test of a phase (never suspends the thread): for polling several
+// barriers in turn.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false (and the
 // caller must abandon its work) if kWaitLimitNs elapses first.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
