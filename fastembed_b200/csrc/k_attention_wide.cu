@@ -443,9 +443,14 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                         uint32_t v[32];
                         tmem_ld_x32(tS + c, v);
                         tmem_wait_ld_regs(v);
+                        if (c + 32 <= lim) {  // no masked key in the chunk (all but the row's last)
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (c + i < lim) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+                            for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (c + i < lim) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+                        }
                     }
                     const float tmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale_log2;
                     // Lazy reference max: P = exp2(s - m) with m raised only when a tile's max
@@ -455,23 +460,40 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                     // a row with no kept key yet keeps m = -inf
                     alpha = mx == m_run ? 1.f : (m_run == -INFINITY ? 0.f : fast_exp2w(m_run - mx));
                     const float msub = mx == -INFINITY ? 0.f : mx;
+                    float rs0 = 0.f, rs1 = 0.f;
                     for (int c = 0; c < valid; c += 32) {
                         uint32_t v[32];
                         tmem_ld_x32(tS + c, v);
                         tmem_wait_ld_regs(v);
                         uint32_t pk[16];
+                        if (c + 32 <= lim) {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float p0 =
-                                c + 2 * i < lim ? fast_exp2w(fmaf(__uint_as_float(v[2 * i]), scale_log2, -msub)) : 0.f;
-                            const float p1 = c + 2 * i + 1 < lim
-                                                 ? fast_exp2w(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -msub))
-                                                 : 0.f;
-                            rs += p0 + p1;
-                            pk[i] = pack_bf16x2(p0, p1);
+                            for (int i = 0; i < 16; ++i) {
+                                const float p0 = fast_exp2w(fmaf(__uint_as_float(v[2 * i]), scale_log2, -msub));
+                                const float p1 = fast_exp2w(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -msub));
+                                rs0 += p0;
+                                rs1 += p1;
+                                pk[i] = pack_bf16x2(p0, p1);
+                            }
+                        } else if (c >= lim) {  // every key of the chunk masked
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float p0 =
+                                    c + 2 * i < lim ? fast_exp2w(fmaf(__uint_as_float(v[2 * i]), scale_log2, -msub)) : 0.f;
+                                const float p1 = c + 2 * i + 1 < lim
+                                                     ? fast_exp2w(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -msub))
+                                                     : 0.f;
+                                rs0 += p0;
+                                rs1 += p1;
+                                pk[i] = pack_bf16x2(p0, p1);
+                            }
                         }
                         tmem_st_x16(tS + (c >> 1), pk);
                     }
+                    rs = rs0 + rs1;
                     tmem_wait_st();
                 }
                 // O *= alpha before this item's PV accumulates (needs the previous PV done)
