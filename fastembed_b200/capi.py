@@ -31,7 +31,10 @@ class EncoderConfig(C.Structure):
     _fields_ = [("vocab_size", C.c_int32), ("hidden", C.c_int32), ("layers", C.c_int32),
                 ("heads", C.c_int32), ("intermediate", C.c_int32), ("max_position", C.c_int32),
                 ("type_vocab", C.c_int32), ("layer_norm_eps", C.c_float), ("activation", C.c_int32),
-                ("pooling", C.c_int32)]
+                ("pooling", C.c_int32), ("positions", C.c_int32), ("pad_token_id", C.c_int32)]
+
+
+POSITIONS = {"bert": 0, "xlmr": 1}
 
 
 class RmsEncoderConfig(C.Structure):
@@ -74,6 +77,7 @@ _SIGS = {
     "fe_linear_bf16": ([vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, C.c_int, vp], C.c_int),
     "fe_attention_varlen_bf16": ([vp, vp, i32, i32, i32, i32, vp, i64, vp], C.c_int),
     "fe_embed_layernorm": ([vp, vp, i32, i64, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, vp], C.c_int),
+    "fe_embed_layernorm_xlmr": ([vp, vp, i32, i64, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp, vp, vp], C.c_int),
     "fe_layernorm_dual": ([vp, vp, vp, vp, vp, vp, i64, i32, f32, vp], C.c_int),
     "fe_attention_varlen_gqa_bf16": ([vp, vp, i32, i32, i32, i32, i32, i32, f32, vp, i64, vp], C.c_int),
     "fe_linear_layernorm_workspace_bytes": ([i64, i64, C.POINTER(sz)], C.c_int),

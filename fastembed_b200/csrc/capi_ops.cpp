@@ -222,6 +222,25 @@ fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int3
                 "fe_embed_layernorm");
 }
 
+fe_status fe_embed_layernorm_xlmr(const int32_t *ids, const int32_t *cu_seqlens, int32_t batch, int64_t total_tokens,
+                                  const float *word, const float *pos, const float *type, const float *gamma,
+                                  const float *beta, int32_t dim, int32_t vocab, int32_t max_pos, int32_t pad_token_id,
+                                  float eps, float *h32, void *h16, fe_stream_t stream)
+{
+    if (batch < 0 || total_tokens < 0 || vocab <= 0 || max_pos <= 0 || pad_token_id < 0)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm_xlmr: bad shape or pad_token_id");
+    if (!supported_row_dim(dim) || dim == 128)
+        return fail(FE_ERR_UNSUPPORTED, "fe_embed_layernorm_xlmr: dim must be 256, 384, 512, 768, 1024, 1536 or 2048");
+    if (total_tokens == 0) return FE_OK;
+    if (batch == 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm_xlmr: tokens without sentences");
+    if (!ids || !cu_seqlens || !word || !pos || !type || !gamma || !beta || !h32)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_embed_layernorm_xlmr: null pointer");
+    return done(fe::launch_embed_layernorm(ids, cu_seqlens, batch, total_tokens, word, pos, type, gamma, beta, dim,
+                                           vocab, max_pos, eps, h32, h16, reinterpret_cast<cudaStream_t>(stream),
+                                           pad_token_id),
+                "fe_embed_layernorm_xlmr");
+}
+
 fe_status fe_layernorm_dual(const float *x, const float *residual, const float *gamma, const float *beta, float *h32,
                             void *h16, int64_t rows, int32_t dim, float eps, fe_stream_t stream)
 {

@@ -300,7 +300,7 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
         FE_TRY_CUDA(fe::launch_embed_layernorm(ids, cu, batch, T, e->word.as<float>(), e->pos.as<float>(),
                                                e->type.as<float>(), e->emb_g.as<float>(), e->emb_b.as<float>(),
                                                static_cast<int>(D), c.vocab_size, c.max_position, c.layer_norm_eps,
-                                               h32, h16, s));
+                                               h32, h16, s, c.positions == FE_POSITIONS_XLMR ? c.pad_token_id : -1));
     }
     const int act = act_epilogue(c.activation);
     for (int l = 0; l < c.layers; ++l) {
@@ -583,6 +583,14 @@ bool config_ok(const fe_encoder_config *c, std::string &why)
     }
     if (c->hidden % c->heads != 0) {
         why = "Embedding dimension must be divisible by number of heads";
+        return false;
+    }
+    if (c->positions != FE_POSITIONS_BERT && c->positions != FE_POSITIONS_XLMR) {
+        why = "positions must be FE_POSITIONS_BERT or FE_POSITIONS_XLMR";
+        return false;
+    }
+    if (c->positions == FE_POSITIONS_XLMR && c->pad_token_id < 0) {
+        why = "pad_token_id must be >= 0 for the XLM-R position rows";
         return false;
     }
     if (c->hidden / c->heads != 64) {

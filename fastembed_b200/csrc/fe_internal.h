@@ -92,7 +92,8 @@ cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t
 cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
                                    const float *word, const float *pos, const float *type,
                                    const float *g, const float *b, int dim, int vocab,
-                                   int max_pos, float eps, float *h32, void *h16, cudaStream_t s);
+                                   int max_pos, float eps, float *h32, void *h16, cudaStream_t s,
+                                   int pad_id = -1);
 // h = LayerNorm(x [+ res]); res may be null, h32 may alias res.
 cudaError_t launch_layernorm_dual(const float *x, const float *res, const float *g, const float *b,
                                   float *h32, void *h16, int64_t rows, int dim, float eps, cudaStream_t s);

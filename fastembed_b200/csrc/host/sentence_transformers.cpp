@@ -168,10 +168,16 @@ public:
         std::string type = "bge";
         if (cfg.has("model_type")) type = cfg.at("model_type").as_string();
         else if (cfg.has("model") && cfg.at("model").has("model_type")) type = cfg.at("model").at("model_type").as_string();
-        if (type != "bge" && type != "bert")
-            throw std::runtime_error("model type '" + type +
-                                     "' needs the XLM-R SentencePiece tokenizer, which this build does not include");
+        // (:64-72) "bge" / "bert" -> BGE; "bge-m3" / "xlm-roberta" -> BGE_M3; anything else
+        // is taken as BGE_M3 with a warning
+        const bool bert = type == "bge" || type == "bert";
+        if (!bert && type != "bge-m3" && type != "xlm-roberta")
+            std::cerr << "warning: unknown model_type '" << type << "', using bge-m3" << std::endl;
         fe_encoder_config c{};
+        if (!bert) {  // position rows of create_position_ids_from_input_ids (:101-123, :139-155)
+            c.positions = FE_POSITIONS_XLMR;
+            c.pad_token_id = cfg_int(cfg, "pad_token_id", 0);
+        }
         c.vocab_size = cfg_int(cfg, "vocab_size", 0);
         c.hidden = cfg_int(cfg, "hidden_size", 0);
         c.layers = cfg_int(cfg, "num_hidden_layers", 0);
@@ -187,7 +193,9 @@ public:
         else throw std::runtime_error("Unsupported activation function");  // (:413-421)
         c.pooling = FE_POOL_CLS;
         cfg_ = c;
-        tokenizer_.reset(new WordPiece(model_path + "/vocab.txt"));
+        // bge-m3 tokenises with SentencePiece (tokenizer.cpp:176-301), which this build does
+        // not include: such models take token ids through encode_ids
+        if (bert) tokenizer_.reset(new WordPiece(model_path + "/vocab.txt"));
 
         for (int dev : devices()) {
             check(cudaSetDevice(dev) == cudaSuccess ? FE_OK : FE_ERR_CUDA, "cudaSetDevice");
@@ -210,6 +218,9 @@ public:
 
     std::vector<int32_t> tokenize(const std::string &text) const
     {
+        if (!tokenizer_)
+            throw std::runtime_error("bge-m3 / XLM-R text needs the SentencePiece tokenizer, which this build does not "
+                                     "include; pass token ids (<s> ... </s>) to encode_ids");
         std::vector<int32_t> ids = tokenizer_->ids(text);
         ids.insert(ids.begin(), 101);
         ids.push_back(102);

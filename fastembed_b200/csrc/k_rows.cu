@@ -50,13 +50,17 @@ __device__ __forceinline__ void ln_store(float4 (&x)[VPT], const float *__restri
     }
 }
 
-// Token t of sentence s: x = word[id] + pos[t - start(s)] + type[0] (summed in that
-// order, src/sentence_transformers_impl.cpp:30-44, :155-188), then LayerNorm (:189-194).
+// Token t of sentence s: x = word[id] + pos[row] + type[0] (summed in that order,
+// src/sentence_transformers_impl.cpp:30-44, :139-188), then LayerNorm (:189-194).  The
+// position row is t - start(s) (BERT), or with pad_id >= 0 the bge-m3 / XLM-R row
+// (:101-123, :146-149): 0 for a token equal to pad_id, else 2 + the number of non-pad
+// tokens before it in the sentence (counted by the warp, 32 ids per step), a row at or
+// past max_pos becoming 0.
 template <int VPT>
 __global__ void __launch_bounds__(256)
     embed_ln(const int32_t *__restrict__ ids, const int32_t *__restrict__ cu, int batch, int64_t total,
              const float *__restrict__ word, const float *__restrict__ pos, const float *__restrict__ type,
-             const float *__restrict__ g, const float *__restrict__ b, int vocab, int max_pos, float eps,
+             const float *__restrict__ g, const float *__restrict__ b, int vocab, int max_pos, int pad_id, float eps,
              float *__restrict__ h32, __nv_bfloat16 *__restrict__ h16, int *status)
 {
     constexpr int dim = 128 * VPT;
@@ -69,8 +73,17 @@ __global__ void __launch_bounds__(256)
         const int mid = (lo + hi + 1) >> 1;
         if (cu[mid] <= t) lo = mid; else hi = mid - 1;
     }
-    const int p = static_cast<int>(t - cu[lo]);
     const int id = ids[t];
+    int p = static_cast<int>(t - cu[lo]);
+    if (pad_id >= 0) {
+        int before = 0;  // non-pad tokens in [start(s), t)
+        for (int64_t j0 = cu[lo]; j0 < t; j0 += 32) {
+            const int64_t j = j0 + lane;
+            before += __popc(__ballot_sync(0xffffffffu, j < t && ids[j] != pad_id));
+        }
+        p = id == pad_id ? 0 : 2 + before;
+        if (p >= max_pos) p = 0;
+    }
     float *o32 = h32 + t * dim;
     __nv_bfloat16 *o16 = h16 ? h16 + t * dim : nullptr;
     if (id < 0 || id >= vocab || p < 0 || p >= max_pos) {
@@ -266,7 +279,7 @@ inline unsigned grid_for(int64_t rows, int per_block) { return static_cast<unsig
 cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
                                    const float *word, const float *pos, const float *type,
                                    const float *g, const float *b, int dim, int vocab, int max_pos,
-                                   float eps, float *h32, void *h16, cudaStream_t s)
+                                   float eps, float *h32, void *h16, cudaStream_t s, int pad_id)
 {
     if (total == 0) return cudaSuccess;
     auto *o16 = static_cast<__nv_bfloat16 *>(h16);
@@ -274,7 +287,7 @@ cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int ba
     const unsigned grid = grid_for(total, 8);
     switch (dim) {
 #define FE_EMB(V) \
-    case 128 * V: embed_ln<V><<<grid, 256, 0, s>>>(ids, cu, batch, total, word, pos, type, g, b, vocab, max_pos, eps, h32, o16, st); break;
+    case 128 * V: embed_ln<V><<<grid, 256, 0, s>>>(ids, cu, batch, total, word, pos, type, g, b, vocab, max_pos, pad_id, eps, h32, o16, st); break;
         FE_EMB(2) FE_EMB(3) FE_EMB(4) FE_EMB(6) FE_EMB(8) FE_EMB(12) FE_EMB(16)
 #undef FE_EMB
         default: return cudaErrorInvalidValue;

@@ -119,14 +119,20 @@ def attention_gqa(qkv, cu_seqlens, max_len, q_heads, kv_heads, head_dim, causal,
     return out
 
 
-def embed_layernorm(ids, cu_seqlens, word, pos, type_, gamma, beta, eps):
+def embed_layernorm(ids, cu_seqlens, word, pos, type_, gamma, beta, eps, pad_id=None):
+    """pad_id None: BERT position rows; an int: the bge-m3 / XLM-R rows with that pad id."""
     _cuda(ids, cu_seqlens, word, pos, type_, gamma, beta)
     T = ids.numel()
     D = word.shape[1]
     h32 = torch.empty(T, D, dtype=torch.float32, device=ids.device)
     h16 = torch.empty(T, D, dtype=torch.bfloat16, device=ids.device)
-    call("fe_embed_layernorm", _p(ids), _p(cu_seqlens), cu_seqlens.numel() - 1, T, _p(word), _p(pos), _p(type_),
-         _p(gamma), _p(beta), D, word.shape[0], pos.shape[0], eps, _p(h32), _p(h16), _s(ids))
+    if pad_id is None:
+        call("fe_embed_layernorm", _p(ids), _p(cu_seqlens), cu_seqlens.numel() - 1, T, _p(word), _p(pos),
+             _p(type_), _p(gamma), _p(beta), D, word.shape[0], pos.shape[0], eps, _p(h32), _p(h16), _s(ids))
+    else:
+        call("fe_embed_layernorm_xlmr", _p(ids), _p(cu_seqlens), cu_seqlens.numel() - 1, T, _p(word), _p(pos),
+             _p(type_), _p(gamma), _p(beta), D, word.shape[0], pos.shape[0], pad_id, eps, _p(h32), _p(h16),
+             _s(ids))
     return h32, h16
 
 
@@ -238,8 +244,10 @@ class Engine:
                                         shape.full_every, 0.0, POOL[shape.pooling])
             capi.check(capi.lib().fe_engine_create_rms(C.byref(cfg), device, C.byref(h)), "fe_engine_create_rms")
         else:
+            pad_id = getattr(shape, "pad_id", -1)  # >= 0: the bge-m3 / XLM-R position rows
             cfg = capi.EncoderConfig(shape.vocab, shape.hidden, shape.layers, shape.heads, shape.intermediate,
-                                     shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], POOL[pooling])
+                                     shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], POOL[pooling],
+                                     capi.POSITIONS["xlmr" if pad_id >= 0 else "bert"], max(pad_id, 0))
             capi.check(capi.lib().fe_engine_create(C.byref(cfg), device, C.byref(h)), "fe_engine_create")
         self._cfg = cfg
         self.h = h

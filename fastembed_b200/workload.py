@@ -38,6 +38,7 @@ class EncoderShape:
     batch: int = 8
     lengths: tuple = ("uniform", 16, 128)
     pad_to: int = 128
+    pad_id: int = -1  # >= 0: bge-m3 / XLM-R position rows with this pad_token_id
 
     @property
     def head_dim(self) -> int:
@@ -164,8 +165,9 @@ def make_weights(shape: EncoderShape, seed: int = 0, std: float = 0.02) -> dict[
 def config_json(shape: EncoderShape) -> dict:
     """The config.json keys the reference reads (src/sentence_transformers_impl.cpp:47-98,
     :189, :199, :240, :268, :413)."""
+    xlmr = shape.pad_id >= 0
     return {
-        "model_type": "bert",
+        "model_type": "xlm-roberta" if xlmr else "bert",
         "vocab_size": shape.vocab,
         "hidden_size": shape.hidden,
         "num_hidden_layers": shape.layers,
@@ -175,7 +177,7 @@ def config_json(shape: EncoderShape) -> dict:
         "layer_norm_eps": shape.eps,
         "max_position_embeddings": shape.max_pos,
         "type_vocab_size": shape.type_vocab,
-        "pad_token_id": 0,
+        "pad_token_id": shape.pad_id if xlmr else 0,
     }
 
 

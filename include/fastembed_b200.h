@@ -174,6 +174,14 @@ fe_status fe_embed_layernorm(const int32_t *ids, const int32_t *cu_seqlens, int3
                              const float *type, const float *gamma, const float *beta,
                              int32_t dim, int32_t vocab, int32_t max_pos, float eps,
                              float *h32, void *h16, fe_stream_t stream);
+/* The same with the bge-m3 / XLM-R position rows (FE_POSITIONS_XLMR above), replacing
+ * the BGE_M3 branch of bge_forward's embedding (src/sentence_transformers_impl.cpp:139-155
+ * with create_position_ids_from_input_ids, :101-123).  Requires pad_token_id >= 0. */
+fe_status fe_embed_layernorm_xlmr(const int32_t *ids, const int32_t *cu_seqlens, int32_t batch,
+                                  int64_t total_tokens, const float *word, const float *pos,
+                                  const float *type, const float *gamma, const float *beta,
+                                  int32_t dim, int32_t vocab, int32_t max_pos, int32_t pad_token_id,
+                                  float eps, float *h32, void *h16, fe_stream_t stream);
 /* h = LayerNorm(x + residual) (residual may be NULL) writing fp32 and (when
  * h16 != NULL) bf16 copies: the residual add and post-residual norms of
  * src/sentence_transformers_impl.cpp:255-266 and :429-437.  h32 may alias residual. */
@@ -227,11 +235,20 @@ fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, i
 /* --------------------------------------------------------- model engine
  * Device-resident post-LN BERT encoder (the reference's bge_forward,
  * src/sentence_transformers_impl.cpp:126-344, batched and packed). */
+/* Position rows of the embedding (src/sentence_transformers_impl.cpp:139-163):
+ *   FE_POSITIONS_BERT  token i of a sentence takes row i (model_type "bge" / "bert");
+ *   FE_POSITIONS_XLMR  bge-m3 / XLM-R (model_type "bge-m3" / "xlm-roberta", :101-123,
+ *                      :146-149): a token equal to pad_token_id takes row 0, the others
+ *                      rows 2, 3, ... in order; a row at or past max_position becomes 0. */
+typedef enum fe_positions { FE_POSITIONS_BERT = 0, FE_POSITIONS_XLMR = 1 } fe_positions;
+
 typedef struct fe_encoder_config {
     int32_t vocab_size, hidden, layers, heads, intermediate, max_position, type_vocab;
     float layer_norm_eps;
     int32_t activation; /* fe_activation */
     int32_t pooling;    /* fe_pooling */
+    int32_t positions;  /* fe_positions (0, the BERT rows, when zero-initialised) */
+    int32_t pad_token_id; /* FE_POSITIONS_XLMR only: config.json pad_token_id (0 if absent, :141) */
 } fe_encoder_config;
 
 /* Pre-RMSNorm rotary encoders, the Qwen3 and Gemma3 shapes (not in the reference; the

@@ -173,9 +173,27 @@ void fe_oracle_mha(const float *x, const float *wq, const float *wk, const float
     free(q); free(k); free(v); free(qh); free(kt); free(vh); free(s); free(p); free(oh);
 }
 
+/* src/sentence_transformers_impl.cpp:101-123 (create_position_ids_from_input_ids: the
+ * count starts at 2, a pad token keeps 0) and :146-149 (a row outside the table is
+ * replaced by row 0). */
+void fe_oracle_position_rows(const int32_t *ids, int len, int pad_id, int max_pos, int32_t *rows)
+{
+    int next = 2;
+    for (int t = 0; t < len; ++t) {
+        if (pad_id < 0) {
+            rows[t] = t;
+            continue;
+        }
+        int r = ids[t] != pad_id ? next++ : 0;
+        if (r < 0 || r >= max_pos) r = 0;
+        rows[t] = r;
+    }
+}
+
 /* Embedding + encoder + CLS/L2 for one unpadded sentence, following
  * src/sentence_transformers_impl.cpp op for op:
- *   :30-44 word gather; :155-163 += position row i; :166-188 += token-type row 0;
+ *   :30-44 word gather; :139-163 += position row (row i, or the bge-m3 rows of
+ *   fe_oracle_position_rows); :166-188 += token-type row 0;
  *   :189-194 LayerNorm(eps);
  *   per layer :199-281: MHA (:243-246) -> out-proj (:250-252) -> += bias (:255-257)
  *     -> += residual (:261-263) -> LayerNorm (:266) -> FFN (:389-440: GEMM1, += b1,
@@ -196,7 +214,11 @@ int fe_oracle_bert_forward(const fe_oracle_bert *m, const int32_t *ids, int len,
     float *hact = malloc(sizeof(float) * L * F);
 
     for (size_t t = 0; t < L; ++t) memcpy(x + t * D, m->word + (size_t)ids[t] * D, sizeof(float) * D);
-    for (size_t i = 0; i < L * D; ++i) x[i] += m->pos[i];
+    int32_t *prow = malloc(sizeof(int32_t) * L);
+    fe_oracle_position_rows(ids, len, m->pad_id, m->max_pos, prow);
+    for (size_t t = 0; t < L; ++t)
+        for (size_t j = 0; j < D; ++j) x[t * D + j] += m->pos[(size_t)prow[t] * D + j];
+    free(prow);
     for (size_t t = 0; t < L; ++t)
         for (size_t j = 0; j < D; ++j) x[t * D + j] += m->type[j];
     fe_oracle_layer_norm(x, m->emb_ln_g, m->emb_ln_b, x, L * D, D, m->eps);

@@ -43,7 +43,14 @@ typedef struct fe_oracle_bert {
     float eps; /* config.json layer_norm_eps */
     const float *word, *pos, *type, *emb_ln_g, *emb_ln_b;
     const fe_oracle_layer *layer; /* [layers] */
+    int pad_id; /* -1: position row i for token i (BERT / BGE); >= 0: the bge-m3 / XLM-R
+                 * rows of fe_oracle_position_rows with this pad_token_id */
 } fe_oracle_bert;
+
+/* Position rows of one sentence (src/sentence_transformers_impl.cpp:101-123, :139-155):
+ * pad_id < 0: row t; pad_id >= 0: a token equal to pad_id takes row 0, the others rows
+ * 2, 3, ... in order, and a row at or past max_pos becomes row 0. */
+void fe_oracle_position_rows(const int32_t *ids, int len, int pad_id, int max_pos, int32_t *rows);
 
 /* --- op-level restatements (src/ops/cpu/cpu_matrix_ops.cpp) --- */
 void fe_oracle_matmul_nt(const float *a, const float *b, float *c, size_t m, size_t n, size_t k);

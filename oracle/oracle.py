@@ -37,7 +37,7 @@ class Bert(C.Structure):
                 ("type_vocab", C.c_int), ("act", C.c_int), ("eps", C.c_float),
                 ("word", C.POINTER(C.c_float)), ("pos", C.POINTER(C.c_float)),
                 ("type", C.POINTER(C.c_float)), ("emb_ln_g", C.POINTER(C.c_float)),
-                ("emb_ln_b", C.POINTER(C.c_float)), ("layer", C.POINTER(Layer))]
+                ("emb_ln_b", C.POINTER(C.c_float)), ("layer", C.POINTER(Layer)), ("pad_id", C.c_int)]
 
 
 ACTS = {"gelu": 0, "relu": 1, "swish": 2}
@@ -95,6 +95,10 @@ def load(kind: str = "port") -> C.CDLL:
     f = getattr(lib, p + "bert_forward_batch")
     f.argtypes = [C.POINTER(Bert), _i32p, _i32p, C.c_int, C.c_int, _f32p, C.c_int]
     f.restype = C.c_int
+    if kind == "port":
+        f = lib.fe_oracle_position_rows
+        f.argtypes = [_i32p, C.c_int, C.c_int, C.c_int, _i32p]
+        f.restype = None
     if kind == "port" or hasattr(lib, "fe_oracle_fill_uniform_mt19937"):
         g = lib.fe_oracle_fill_uniform_mt19937
         g.argtypes = [C.c_uint32, C.c_float, C.c_float, _f32p, sz]
@@ -163,6 +167,15 @@ def mha(x, wq, wk, wv, bq, bk, bv, heads, dim, kind="port"):
     return out
 
 
+def position_rows(ids, pad_id, max_pos):
+    """Position-table rows of one sentence (BERT rows 0..L-1 for pad_id < 0, else the
+    bge-m3 / XLM-R rows)."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    rows = np.empty(ids.size, np.int32)
+    load("port").fe_oracle_position_rows(ids, ids.size, pad_id, max_pos, rows)
+    return rows
+
+
 def uniform_mt19937(count, seed=42, lo=-1.0, hi=1.0):
     """std::mt19937(seed) + uniform_real_distribution<float>(lo, hi): the generator
     of the reference's GTest inputs (tests/*_ops_test.cpp)."""
@@ -198,7 +211,7 @@ class Model:
                            P("embeddings.position_embeddings.weight"),
                            P("embeddings.token_type_embeddings.weight"),
                            P("embeddings.LayerNorm.weight"), P("embeddings.LayerNorm.bias"),
-                           C.cast(layers, C.POINTER(Layer)))
+                           C.cast(layers, C.POINTER(Layer)), getattr(shape, "pad_id", -1))
 
     def forward(self, ids, kind="port"):
         ids = np.ascontiguousarray(ids, dtype=np.int32)

@@ -32,11 +32,21 @@ int forward_one(const fe_oracle_bert *m, const int32_t *ids, int len, float *out
     CPUMatrixOps mops;
     CPUAttentionOps aops;
 
-    // word gather (:30-44), += position row i (:155-163), += token type 0 (:166-188)
+    // word gather (:30-44), += position row (:139-163), += token type 0 (:166-188).
+    // bge-m3 / XLM-R rows (:101-123, :146-149): pad tokens row 0, the others 2, 3, ...;
+    // a row outside the table becomes row 0.
     std::vector<float> x(L * D);
     for (size_t t = 0; t < L; ++t)
         std::memcpy(&x[t * D], m->word + (size_t)ids[t] * D, sizeof(float) * D);
-    for (size_t i = 0; i < L * D; ++i) x[i] += m->pos[i];
+    int next_row = 2;
+    for (size_t t = 0; t < L; ++t) {
+        int row = static_cast<int>(t);
+        if (m->pad_id >= 0) {
+            row = ids[t] == m->pad_id ? 0 : next_row++;
+            if (row >= m->max_pos) row = 0;
+        }
+        for (size_t j = 0; j < D; ++j) x[t * D + j] += m->pos[(size_t)row * D + j];
+    }
     for (size_t t = 0; t < L; ++t)
         for (size_t j = 0; j < D; ++j) x[t * D + j] += m->type[j];
     x = mops.layer_norm(x, vec(m->emb_ln_g, D), vec(m->emb_ln_b, D), D, m->eps);

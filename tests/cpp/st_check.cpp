@@ -6,6 +6,9 @@
 // reads one text per line and writes <out_prefix>.ids (per text: int32 count, then the
 // ids), <out_prefix>.batch (float32 [n, dim] from encode_batch) and <out_prefix>.single
 // (float32 [n, dim] from encode, one text at a time).
+//   st_check <model_dir> <ids_file> <out_prefix> ids
+// reads token ids in the .ids format and writes <out_prefix>.batch from encode_ids (the
+// path of models whose tokenizer this build does not include, e.g. bge-m3).
 #include <cstdint>
 #include <cstdio>
 #include <fstream>
@@ -17,12 +20,33 @@
 
 int main(int argc, char **argv)
 {
-    if (argc != 4) {
-        std::fprintf(stderr, "usage: st_check <model_dir> <texts_file> <out_prefix>\n");
+    if (argc != 4 && !(argc == 5 && std::string(argv[4]) == "ids")) {
+        std::fprintf(stderr, "usage: st_check <model_dir> <texts_file> <out_prefix> [ids]\n");
         return 2;
     }
     try {
         SentenceTransformer model(argv[1]);
+        if (argc == 5) {
+            std::ifstream in(argv[2], std::ios::binary);
+            std::vector<std::vector<int32_t>> seqs;
+            for (int32_t n = 0; in.read(reinterpret_cast<char *>(&n), 4);) {
+                std::vector<int32_t> v(n);
+                in.read(reinterpret_cast<char *>(v.data()), 4 * n);
+                seqs.push_back(v);
+            }
+            std::ofstream batch(std::string(argv[3]) + ".batch", std::ios::binary);
+            for (const auto &e : model.encode_ids(seqs))
+                batch.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());
+            bool threw = false;  // text needs the SentencePiece tokenizer, absent from this build
+            try {
+                (void)model.tokenize("text");
+            } catch (const std::exception &) {
+                threw = true;
+            }
+            std::printf("dim %zu, %zu id sequences, text rejected %d\n", model.get_embedding_dimension(), seqs.size(),
+                        threw ? 1 : 0);
+            return 0;
+        }
         std::vector<std::string> texts;
         std::ifstream in(argv[2]);
         for (std::string line; std::getline(in, line);) texts.push_back(line);

@@ -100,3 +100,31 @@ def test_multi_engine_slices_are_bit_identical(cuda_dev, tmp_path):
     _, _, _, _, one, _ = _run_model(tmp_path / "one", "F32")
     _, _, _, _, two, _ = _run_model(tmp_path / "two", "F32", {"FE_DEVICES": "0,0"})
     assert np.array_equal(one, two)
+
+
+def test_sentence_transformer_bge_m3_ids(cuda_dev, oracle_lib, tmp_path):
+    """A bge-m3 model directory (model_type "xlm-roberta", pad_token_id 1) through the C++
+    SentenceTransformer: encode_ids matches the oracle's XLM-R position path, and text is
+    refused (the SentencePiece tokenizer is not part of this build)."""
+    from fastembed_b200 import workload as W
+    from tests.model_dir import write_model_dir
+    shape = dataclasses.replace(W.SHAPES["bge-small"], layers=2, max_pos=64, type_vocab=1, pad_id=1)
+    weights = W.make_weights(shape, seed=31)
+    mdir = str(tmp_path / "m3")
+    write_model_dir(mdir, shape, weights, "F32")
+    lengths = np.array([3, 9, 60, 64, 20], np.int32)
+    ids, _ = W.sample_ids(shape, lengths, seed=32, pad_to=64)
+    ids[1, 4] = 1
+    ids[4, 2:6] = 1
+    seqs = [ids[b, :lengths[b]] for b in range(len(lengths))]
+    raw = np.concatenate([np.concatenate([[len(x)], x]) for x in seqs]).astype(np.int32)
+    (tmp_path / "ids.bin").write_bytes(raw.tobytes())
+    pre = str(tmp_path / "out")
+    r = subprocess.run([_st_check(), mdir, str(tmp_path / "ids.bin"), pre, "ids"], capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr
+    assert "text rejected 1" in r.stdout
+    got = np.fromfile(pre + ".batch", dtype=np.float32).reshape(-1, shape.hidden)
+    ref = oracle_lib.Model(shape, weights).forward_batch(ids, lengths)
+    cos = (got * ref).sum(1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(ref, axis=1))
+    assert cos.min() >= 0.9999 and np.abs(got - ref).max() <= 2e-3

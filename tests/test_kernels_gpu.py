@@ -241,6 +241,36 @@ def test_layernorm_dual(cuda_dev):
             assert torch.equal(h16r, h32r.to(torch.bfloat16))
 
 
+def test_embed_layernorm_xlmr_rows(cuda_dev):
+    """fe_embed_layernorm_xlmr: pad tokens take position row 0, the others rows 2, 3, ... of
+    their sentence, a row at or past the table row 0; against the fp32 torch composition."""
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(5)
+    D, V, P, pad = 768, 300, 40, 1
+    lens = [1, 3, 38, 39, 45, 17]
+    T = sum(lens)
+    ids = torch.randint(0, 6, (T,), device=cuda_dev, generator=g).to(torch.int32)  # many pads
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    word = torch.randn(V, D, device=cuda_dev, generator=g)
+    pos = torch.randn(P, D, device=cuda_dev, generator=g)
+    typ = torch.randn(1, D, device=cuda_dev, generator=g)
+    gam = torch.randn(D, device=cuda_dev, generator=g)
+    bet = torch.randn(D, device=cuda_dev, generator=g)
+    h32, h16 = ops.embed_layernorm(ids, cu, word, pos, typ, gam, bet, 1e-5, pad_id=pad)
+    rows, host = [], ids.cpu().numpy()
+    for s, L in zip(np.cumsum([0] + lens[:-1]), lens):
+        nxt = 2
+        for t in range(s, s + L):
+            r = 0 if host[t] == pad else nxt
+            nxt += int(host[t] != pad)
+            rows.append(r if r < P else 0)
+    x = word[ids.long()] + pos[torch.tensor(rows, device=cuda_dev)] + typ[0]
+    ref = torch.nn.functional.layer_norm(x, (D,), gam, bet, 1e-5)
+    assert float((h32 - ref).abs().max()) < 1e-4
+    assert torch.equal(h16, h32.to(torch.bfloat16))
+    ops.device_status(0)
+
+
 # ----------------------------------------- linear + residual + LayerNorm, one launch
 def _linear_ln_ref(x, w, b, res, gam, bet, eps):
     y = (x.float() @ w.float().T + b) + res

@@ -114,3 +114,26 @@ def test_full_batch_properties_bge_large(cuda_dev):
     d = eng.encode_host(ids[17:40], lengths[17:40])
     assert np.array_equal(d, a[17:40])
     eng.close()
+
+
+def test_xlmr_positions_match_oracle(cuda_dev, oracle_lib):
+    """bge-m3 / XLM-R position rows (model_type "xlm-roberta", pad_token_id 1): pad ids
+    inside sentences take row 0, the others rows 2, 3, ...; rows past the 48-row table
+    become row 0 (sentence_transformers_impl.cpp:101-123, :139-155)."""
+    from fastembed_b200 import ops, workload as W
+    import dataclasses
+    shape = dataclasses.replace(W.SHAPES["bge-small"], layers=2, max_pos=48, type_vocab=1, pad_id=1)
+    weights = W.make_weights(shape, seed=21)
+    lengths = np.array([1, 2, 5, 33, 46, 47, 48, 40], np.int32)
+    ids, _ = W.sample_ids(shape, lengths, seed=22, pad_to=48)
+    ids[2, 2] = 1
+    ids[3, [0, 7, 8, 30]] = 1
+    ids[7, 5:25] = 1
+    ref = oracle_lib.Model(shape, weights).forward_batch(ids, lengths)
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(weights)
+    got = eng.encode_host(ids, lengths)
+    _check(got, ref)
+    for b in (3, 7):  # batch invariance, bit for bit
+        assert np.array_equal(eng.encode_host(ids[b:b + 1], lengths[b:b + 1])[0], got[b])
+    eng.close()

@@ -123,3 +123,48 @@ def test_forward_rejects_overlong_and_bad_ids(oracle_lib):
         m.forward(np.full(17, 120, np.int32))
     with pytest.raises(ValueError):
         m.forward(np.array([101, 300, 102], np.int32))
+
+
+def test_xlmr_position_rows(oracle_lib):
+    """bge-m3 / XLM-R rows (src/sentence_transformers_impl.cpp:101-123, :146-149): pad tokens
+    row 0, the others 2, 3, ... in order, a row at or past the table row 0; BERT rows 0..L-1."""
+    O = oracle_lib
+    ids = np.array([0, 5, 1, 7, 1, 1, 9, 2], np.int32)
+    assert O.position_rows(ids, -1, 512).tolist() == list(range(8))
+    assert O.position_rows(ids, 1, 512).tolist() == [2, 3, 0, 4, 0, 0, 5, 6]
+    assert O.position_rows(ids, 0, 512).tolist() == [0, 2, 3, 4, 5, 6, 7, 8]
+    assert O.position_rows(ids, 1, 5).tolist() == [2, 3, 0, 4, 0, 0, 0, 0]  # rows >= 5 become 0
+    rng = np.random.default_rng(3)
+    for _ in range(50):
+        L, pad, maxp = int(rng.integers(1, 60)), int(rng.integers(0, 4)), int(rng.integers(2, 70))
+        x = rng.integers(0, 4, L).astype(np.int32)
+        want, nxt = [], 2
+        for v in x:
+            r = 0 if v == pad else nxt
+            nxt += v != pad
+            want.append(r if r < maxp else 0)
+        assert O.position_rows(x, pad, maxp).tolist() == want
+
+
+def test_port_equals_reference_forward_xlmr(oracle_lib):
+    """The bge-m3 position path of the port equals the reference-ops driver bit for bit,
+    with pad ids inside sentences and rows running past the table."""
+    O = oracle_lib
+    if not O.available("ref"):
+        pytest.skip("oracle/_ref not built here")
+    import dataclasses
+    from fastembed_b200 import workload as W
+    shape = dataclasses.replace(W.SHAPES["bge-small"], layers=2, hidden=256, heads=4, intermediate=512,
+                                vocab=500, max_pos=48, type_vocab=1, pad_id=1)
+    w = W.make_weights(shape, seed=8)
+    lengths = np.array([1, 3, 17, 48], np.int32)
+    ids, _ = W.sample_ids(shape, lengths, seed=9, pad_to=48)
+    ids[1, 1] = 1
+    ids[2, [0, 5, 6]] = 1
+    ids[3, 10:14] = 1
+    m = O.Model(shape, w)
+    got = m.forward_batch(ids, lengths)
+    assert np.array_equal(got, m.forward_batch(ids, lengths, kind="ref"))
+    # the rows differ from the BERT ones, so the outputs do
+    bert = O.Model(dataclasses.replace(shape, pad_id=-1), w).forward_batch(ids, lengths)
+    assert not np.allclose(got, bert)
