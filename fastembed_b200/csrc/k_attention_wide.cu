@@ -12,9 +12,10 @@
 //              item, each as head_dim / 64 boxes of 128 rows x 128 bytes (128B swizzle);
 //              K and V advance independently, and the next unit's tiles are prefetched
 //              into L2 (measured on the Qwen3-0.6B shape, 71,550 tokens: 648 -> 557 us).
-//   warp 1     MMA issuer: S = Q K^T (K = head_dim) into an S slot; O (+)= P V with P
-//              (bf16) read from TMEM and V an MN-major operand, issued as soon as P is
-//              written; the first item of a unit overwrites O.
+//   warp 1     MMA issuer: S = Q K^T (K = head_dim) into an S slot; for the previous item
+//              O (+)= P V with P (bf16) read from TMEM and V an MN-major operand; the
+//              first item of a unit overwrites O.  (Issuing each PV as soon as its P is
+//              written, from a polled queue, measured 1 % slower.)
 //   warps 2-5  softmax (thread = query row): masked online softmax over S, P written back
 //              over S; when a row's reference max rises (by more than 2^8 in P), O is
 //              rescaled in TMEM after the previous item's PV and before this one's; O / l
@@ -289,69 +290,39 @@ __global__ void __launch_bounds__(kThreadsW, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
-            // S MMAs are issued in item order, each as soon as its K tile and S slot are
-            // ready; the PV MMAs (queued, at most two) as soon as their P is written, so a
-            // PV never waits behind the K load of a later item.  Barriers are polled with
-            // non-suspending tests, so that no wait on one holds up another that completed.
             constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
             uint32_t qn = 0, kvn = 0, it = 0, un = 0;
-            bool ok = true, issued = false;
-            struct Pend {
-                uint32_t it, ks, kvn, o, un;
-                int valid;
-                bool first;
-            };
-            Pend pq[2];
-            int np = 0;  // queued PVs, oldest first
-            auto pv_ready = [&]() -> bool {
-                const Pend &pp = pq[0];
-                if (pp.first && !mbar_test_wait(&o_free[pp.o], ((pp.un / OS) & 1) ^ 1)) return false;
-                if (!mbar_test_wait(&p_full[pp.it & 1], (pp.it >> 1) & 1)) return false;
-                return mbar_test_wait(&v_full[pp.ks], (pp.kvn / KVS) & 1);
-            };
-            // O(o) (+)= P(slot) V for the oldest queued item (P from TMEM, V MN-major: 16 keys = 2048 bytes a step)
-            auto issue_pv = [&]() {
-                const Pend pp = pq[0];
-                pq[0] = pq[1];
-                --np;
-                const uint32_t b = pp.it & 1;
+            bool ok = true, issued = false, have_pend = false;
+            uint32_t pend_it = 0, pend_ks = 0, pend_kvn = 0, pend_o = 0, pend_un = 0;
+            int pend_valid = 0;
+            bool pend_first = false;
+            // O(o) (+)= P(slot) V for item `pit` (P from TMEM, V MN-major: 16 keys = 2048 bytes a step)
+            auto issue_pv = [&]() -> bool {
+                const uint32_t b = pend_it & 1;
+                if (pend_first && !wait(&o_free[pend_o], ((pend_un / OS) & 1) ^ 1)) return false;
+                if (!wait(&p_full[b], (pend_it >> 1) & 1)) return false;
+                if (!wait(&v_full[pend_ks], (pend_kvn / KVS) & 1)) return false;
                 tc_fence_after();
-                const uint64_t v_desc = sdesc_sw128(smem_u32(sV + pp.ks * C::TILE), BOX_BYTES, 1024);
-                const uint32_t o_tmem = tmem + 256 + pp.o * HD;
-                const int nks = (pp.valid + 15) >> 4;
+                const uint64_t v_desc = sdesc_sw128(smem_u32(sV + pend_ks * C::TILE), BOX_BYTES, 1024);
+                const uint32_t o_tmem = tmem + 256 + pend_o * HD;
+                const int nks = (pend_valid + 15) >> 4;
                 for (int ks = 0; ks < nks; ++ks)
                     umma_f16_ts(o_tmem, tmem + b * 128 + ks * 8, v_desc + static_cast<uint64_t>(ks * 128), idesc_o,
-                                (pp.first && ks == 0) ? 0u : 1u);
+                                (pend_first && ks == 0) ? 0u : 1u);
                 umma_commit(&pv_done[b]);
                 umma_commit(&s_free[b]);
-                umma_commit(&v_empty[pp.ks]);
-            };
-            // Polls until `ready` holds, issuing queued PVs whose operands are ready meanwhile.
-            auto wait_issuing = [&](auto &&ready) -> bool {
-                const uint64_t t0 = globaltimer_ns();
-                for (uint32_t i = 0;; ++i) {
-                    if (np > 0 && pv_ready()) issue_pv();
-                    if (ready()) return true;
-                    __nanosleep(20);
-                    if ((i & 255u) == 255u && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
-                        report(status, DEV_TIMEOUT);
-                        *abort_flag = 1;
-                        return false;
-                    }
-                }
+                umma_commit(&v_empty[pend_ks]);
+                return true;
             };
             for (int g = blockIdx.x; g < total_units && ok && !*abort_flag; g += gridDim.x) {
                 const U w = unit(g);
                 const int qs = qn % QS;
-                if (!(ok = wait_issuing([&] { return mbar_test_wait(&q_full[qs], (qn / QS) & 1); }))) break;
+                if (!(ok = wait(&q_full[qs], (qn / QS) & 1))) break;
                 for (int j = 0; j < w.n_kv; ++j) {
                     const uint32_t ks = kvn % KVS;
                     const uint32_t b = it & 1;
-                    if (!(ok = wait_issuing([&] {
-                              return mbar_test_wait(&k_full[ks], (kvn / KVS) & 1) &&
-                                     mbar_test_wait(&s_free[b], ((it >> 1) & 1) ^ 1);
-                          })))
-                        break;
+                    if (!(ok = wait(&k_full[ks], (kvn / KVS) & 1))) break;
+                    if (!(ok = wait(&s_free[b], ((it >> 1) & 1) ^ 1))) break;
                     tc_fence_after();
                     const int valid = min(TK, w.len - j * TK);
                     const int n = min(TK, max(16, (valid + 15) & ~15));
@@ -367,15 +338,22 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                     umma_commit(&s_full[b]);
                     umma_commit(&k_empty[ks]);
                     if (j == w.n_kv - 1) umma_commit(&q_empty[qs]);
-                    // S(it) waited for s_free of slot b, i.e. for PV(it - 2): at most PV(it - 1) is queued
-                    pq[np++] = Pend{it, ks, kvn, un % OS, un, valid, j == 0};
+                    if (have_pend && !(ok = issue_pv())) break;
+                    have_pend = true;
+                    pend_it = it;
+                    pend_ks = ks;
+                    pend_kvn = kvn;
+                    pend_o = un % OS;
+                    pend_un = un;
+                    pend_valid = valid;
+                    pend_first = j == 0;
                     ++it;
                     ++kvn;
                 }
                 ++qn;
                 ++un;
             }
-            if (ok && np > 0 && !*abort_flag) ok = wait_issuing([&] { return np == 0; });
+            if (ok && have_pend && !*abort_flag) ok = issue_pv();
             if (issued) {
                 umma_commit(probe);
                 (void)mbar_wait(probe, 0);
