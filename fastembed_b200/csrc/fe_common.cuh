@@ -470,6 +470,16 @@ __device__ __forceinline__ float gelu_tanh_fast(float x)
     return fmaf(h, t, h);
 }
 
+// a += c, b += d as one packed f32x2 add (round to nearest, as the scalar adds)
+__device__ __forceinline__ void add_f32x2(float &a, float &b, float c, float d)
+{
+    unsigned long long x, y;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(c), "f"(d));
+    asm("add.rn.f32x2 %0, %0, %1;" : "+l"(x) : "l"(y));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+
 // gelu_tanh_fast of two values with the packed f32x2 FP32 instructions of sm_100 (the
 // same operations per lane, so the results equal the scalar form's).
 __device__ __forceinline__ void gelu_tanh_fast2(float &a, float &b)

@@ -135,10 +135,8 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
 #pragma unroll
                 for (int j = 0; j < CHUNK; j += 4) {
                     const float4 bb = __ldg(reinterpret_cast<const float4 *>(bias + col0 + j));
-                    f[j] += bb.x;
-                    f[j + 1] += bb.y;
-                    f[j + 2] += bb.z;
-                    f[j + 3] += bb.w;
+                    add_f32x2(f[j], f[j + 1], bb.x, bb.y);
+                    add_f32x2(f[j + 2], f[j + 3], bb.z, bb.w);
                 }
             } else {
 #pragma unroll
@@ -153,10 +151,8 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
 #pragma unroll
                     for (int j = 0; j < CHUNK; j += 4) {
                         const float4 rr = __ldg(reinterpret_cast<const float4 *>(rp + j));
-                        f[j] += rr.x;
-                        f[j + 1] += rr.y;
-                        f[j + 2] += rr.z;
-                        f[j + 3] += rr.w;
+                        add_f32x2(f[j], f[j + 1], rr.x, rr.y);
+                        add_f32x2(f[j + 2], f[j + 3], rr.z, rr.w);
                     }
                 } else {
 #pragma unroll
