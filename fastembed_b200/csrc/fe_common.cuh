@@ -470,6 +470,25 @@ __device__ __forceinline__ float gelu_tanh_fast(float x)
     return fmaf(h, t, h);
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max)
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// (a, b) <- (xa * y + z, xb * y + z) as one packed f32x2 fma (each lane an IEEE fma)
+__device__ __forceinline__ void fma_f32x2(float &a, float &b, float xa, float xb, float y, float z)
+{
+    unsigned long long x, yy, zz, d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(xa), "f"(xb));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(yy) : "f"(y));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(zz) : "f"(z));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(x), "l"(yy), "l"(zz));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(d));
+}
+
 // a += c, b += d as one packed f32x2 add (round to nearest, as the scalar adds)
 __device__ __forceinline__ void add_f32x2(float &a, float &b, float c, float d)
 {

@@ -445,7 +445,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                         tmem_wait_ld();
                         if (c + 32 <= valid) {
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+                            for (int i = 0; i < 32; i += 2)
+                                m4[(i >> 1) & 3] = max3f(m4[(i >> 1) & 3], __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
                         } else {
 #pragma unroll
                             for (int i = 0; i < 32; ++i)
@@ -462,11 +463,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                         uint32_t pk[16];
                         if (c + 32 <= valid) {
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                const float p0 = fast_exp2(fmaf(__uint_as_float(v[2 * i]), scale_log2, -mx));
-                                const float p1 = fast_exp2(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -mx));
-                                rs0 += p0;
-                                rs1 += p1;
+                            for (int i = 0; i < 16; ++i) {  // packed f32x2: scale and shift, then row sums
+                                float p0, p1;
+                                fma_f32x2(p0, p1, __uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), scale_log2,
+                                          -mx);
+                                p0 = fast_exp2(p0);
+                                p1 = fast_exp2(p1);
+                                add_f32x2(rs0, rs1, p0, p1);
                                 pk[i] = pack_bf16x2(p0, p1);
                             }
                         } else {
