@@ -423,7 +423,8 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                         tmem_wait_ld_regs(v);
                         if (c + 32 <= lim) {  // no masked key in the chunk (all but the row's last)
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(v[i]));
+                            for (int i = 0; i < 32; i += 2)
+                                m4[(i >> 1) & 3] = max3f(m4[(i >> 1) & 3], __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
                         } else {
 #pragma unroll
                             for (int i = 0; i < 32; ++i)
@@ -446,11 +447,13 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                         uint32_t pk[16];
                         if (c + 32 <= lim) {
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                const float p0 = fast_exp2w(fmaf(__uint_as_float(v[2 * i]), scale_log2, -msub));
-                                const float p1 = fast_exp2w(fmaf(__uint_as_float(v[2 * i + 1]), scale_log2, -msub));
-                                rs0 += p0;
-                                rs1 += p1;
+                            for (int i = 0; i < 16; ++i) {  // packed f32x2: scale and shift, then row sums
+                                float p0, p1;
+                                fma_f32x2(p0, p1, __uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), scale_log2,
+                                          -msub);
+                                p0 = fast_exp2w(p0);
+                                p1 = fast_exp2w(p1);
+                                add_f32x2(rs0, rs1, p0, p1);
                                 pk[i] = pack_bf16x2(p0, p1);
                             }
                         } else if (c >= lim) {  // every key of the chunk masked
