@@ -489,6 +489,28 @@ __device__ __forceinline__ void fma_f32x2(float &a, float &b, float xa, float xb
     asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(d));
 }
 
+// (a, b) <- (xa * ya + za, xb * yb + zb) as one packed f32x2 fma
+__device__ __forceinline__ void fma_f32x2v(float &a, float &b, float xa, float xb, float ya, float yb, float za,
+                                           float zb)
+{
+    unsigned long long x, y, z, d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(xa), "f"(xb));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(ya), "f"(yb));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(z) : "f"(za), "f"(zb));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(x), "l"(y), "l"(z));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(d));
+}
+
+// a *= c, b *= d as one packed f32x2 multiply
+__device__ __forceinline__ void mul_f32x2(float &a, float &b, float c, float d)
+{
+    unsigned long long x, y;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(c), "f"(d));
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(x) : "l"(y));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+
 // a += c, b += d as one packed f32x2 add (round to nearest, as the scalar adds)
 __device__ __forceinline__ void add_f32x2(float &a, float &b, float c, float d)
 {
