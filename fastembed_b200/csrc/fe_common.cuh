@@ -521,6 +521,20 @@ __device__ __forceinline__ void add_f32x2(float &a, float &b, float c, float d)
     asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
 }
 
+// silu(a) = a / (1 + e^-a) of two values: e^-a by ex2.approx, the division by
+// rcp.approx (both MUFU), the FP32 arithmetic as packed f32x2 instructions.  Saturates
+// correctly: e^-a = inf gives a * 0, e^-a = 0 gives a.
+__device__ __forceinline__ void silu_fast2(float &a, float &b)
+{
+    float e0 = -1.4426950408889634f * a, e1 = -1.4426950408889634f * b;
+    asm("ex2.approx.ftz.f32 %0, %0;" : "+f"(e0));
+    asm("ex2.approx.ftz.f32 %0, %0;" : "+f"(e1));
+    add_f32x2(e0, e1, 1.0f, 1.0f);
+    asm("rcp.approx.ftz.f32 %0, %0;" : "+f"(e0));
+    asm("rcp.approx.ftz.f32 %0, %0;" : "+f"(e1));
+    mul_f32x2(a, b, e0, e1);
+}
+
 // gelu_tanh_fast of two values with the packed f32x2 FP32 instructions of sm_100 (the
 // same operations per lane, so the results equal the scalar form's).
 __device__ __forceinline__ void gelu_tanh_fast2(float &a, float &b)

@@ -87,10 +87,13 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
                     tmem_wait_ld_regs(g);
                     tmem_wait_ld_regs(u);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float a = __uint_as_float(g[j]);
-                        const float ga = epi == E_SWIGLU ? a / (1.0f + __expf(-a)) : gelu_tanh_fast(a);
-                        o[32 * hb + j] = ga * __uint_as_float(u[j]);
+                    for (int j = 0; j < 32; j += 2) {
+                        float a0 = __uint_as_float(g[j]), a1 = __uint_as_float(g[j + 1]);
+                        if (epi == E_SWIGLU) silu_fast2(a0, a1);
+                        else gelu_tanh_fast2(a0, a1);
+                        mul_f32x2(a0, a1, __uint_as_float(u[j]), __uint_as_float(u[j + 1]));
+                        o[32 * hb + j] = a0;
+                        o[32 * hb + j + 1] = a1;
                     }
                 }
                 uint8_t *buf = bufs + pp * kStageBufBytes;
