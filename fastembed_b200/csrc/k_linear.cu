@@ -166,6 +166,9 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
         } else if (epi == E_GELU) {
 #pragma unroll
             for (int j = 0; j < CHUNK; j += 2) gelu_tanh_fast2(f[j], f[j + 1]);
+        } else if (epi == E_SWISH) {
+#pragma unroll
+            for (int j = 0; j < CHUNK; j += 2) silu_fast2(f[j], f[j + 1]);
         } else if (epi >= E_GELU) {
 #pragma unroll
             for (int j = 0; j < CHUNK; ++j) f[j] = act(f[j], epi);

@@ -37,7 +37,7 @@ LINEAR_SHAPES = [
 @pytest.mark.parametrize("pair", ["1", "0"])
 @pytest.mark.parametrize("m,n,k", LINEAR_SHAPES)
 @pytest.mark.parametrize("epi,out", [("none", "f32"), ("bias", "bf16"), ("bias_gelu", "bf16"),
-                                     ("bias_residual", "f32")])
+                                     ("bias_swish", "bf16"), ("bias_residual", "f32")])
 def test_linear_bf16(cuda_dev, monkeypatch, m, n, k, epi, out, pair):
     """Both linear kernels: the 2-CTA pair kernel (default for m >= 512 and n % 256 == 0)
     and the 1-CTA kernel (FE_LINEAR_PAIR=0)."""
@@ -54,11 +54,13 @@ def test_linear_bf16(cuda_dev, monkeypatch, m, n, k, epi, out, pair):
         ref = ref + bias
     if epi == "bias_gelu":
         ref = 0.5 * ref * (1 + torch.tanh(math.sqrt(2 / math.pi) * (ref + 0.044715 * ref ** 3)))
+    if epi == "bias_swish":
+        ref = ref * torch.sigmoid(ref)
     if epi == "bias_residual":
         ref = ref + res
     torch.cuda.synchronize()
     # fp32 out: only the accumulation order differs -> 1e-4 relative to the output scale;
-    # bf16 out: one bf16 rounding (2^-8 relative) plus the hardware tanh -> 1e-2.
+    # bf16 out: one bf16 rounding (2^-8 relative) plus the hardware tanh / ex2 / rcp -> 1e-2.
     tol = 1e-4 if out == "f32" else 1e-2
     assert _rel_err(y, ref) < tol
     ops.device_status(0)
