@@ -26,6 +26,24 @@ __device__ __forceinline__ int sentence_of(const int32_t *cu, int batch, int64_t
     return lo;
 }
 
+// sin and cos of an angle: Cody-Waite reduction to [-pi, pi] with 2 pi split in two
+// floats (the high part exact in the FMA, the low part the rounding error of the first),
+// then the hardware sin / cos, accurate to about 1e-6 on that interval.  Angles here are
+// position * inverse frequency, below 2^17, where the two-constant reduction is exact to
+// float rounding.
+__device__ __forceinline__ void sincos_reduced(float a, float &s, float &c)
+{
+    constexpr double kTwoPi = 6.283185307179586476925286766559;
+    constexpr float kHi = static_cast<float>(kTwoPi);
+    constexpr float kLo = static_cast<float>(kTwoPi - static_cast<double>(kHi));
+    constexpr float kInv = static_cast<float>(1.0 / kTwoPi);
+    const float k = rintf(a * kInv);
+    float r = fmaf(-k, kHi, a);
+    r = fmaf(-k, kLo, r);
+    s = __sinf(r);
+    c = __cosf(r);
+}
+
 // h32[t] = word[ids[t]] * scale.  Out-of-range ids record FE_ERR_INVALID_ARGUMENT and
 // write zeros.
 template <int VPT>
@@ -181,32 +199,53 @@ __global__ void __launch_bounds__(256)
         const int e = E * lane + i;
         const int fi = e & (HD / 2 - 1);  // frequency index
         const float inv_freq = exp2f(-log2_theta * static_cast<float>(2 * fi) / static_cast<float>(HD));
-        sincosf(static_cast<float>(pos) * inv_freq, &sn[i], &cs[i]);
+        // measured: the reduced hardware form is faster at head_dim 128 (4 angles a lane),
+        // sincosf at 256 (8 angles a lane, 4 heads a token)
+        if constexpr (HD == 128) sincos_reduced(static_cast<float>(pos) * inv_freq, sn[i], cs[i]);
+        else sincosf(static_cast<float>(pos) * inv_freq, &sn[i], &cs[i]);
         wq[i] = q_w[e] + (one_plus ? 1.f : 0.f);
         wk[i] = k_w[e] + (one_plus ? 1.f : 0.f);
     }
     const bool lo = lane < 16;  // elements i < HD/2
     __nv_bfloat16 *row = qkv + t * static_cast<int64_t>(q_heads + 2 * kv_heads) * HD + E * lane;
     const int nh = q_heads + kv_heads;
-#pragma unroll 2
-    for (int h = 0; h < nh; ++h) {
-        __nv_bfloat16 *p = row + h * HD;
-        float x[E];
-        load_head<HD>(p, x);
-        float s = 0.f;
+    // Heads in groups of G: the group's loads are issued together and its G row
+    // reductions run interleaved.
+    constexpr int G = HD == 128 ? 4 : 1;
+#pragma unroll(HD == 128 ? 1 : 2)
+    for (int h0 = 0; h0 < nh; h0 += G) {
+        float x[G][E];
+        float ss[G];
 #pragma unroll
-        for (int i = 0; i < E; ++i) s += x[i] * x[i];
-        const float r = rsqrtf(warp_sum(s) / static_cast<float>(HD) + eps);
-        const bool is_q = h < q_heads;
-#pragma unroll
-        for (int i = 0; i < E; ++i) x[i] = x[i] * r * (is_q ? wq[i] : wk[i]);
-        float y[E];
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-            const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
-            y[i] = lo ? x[i] * cs[i] - partner * sn[i] : x[i] * cs[i] + partner * sn[i];
+        for (int g = 0; g < G; ++g) {
+            ss[g] = 0.f;
+            if (h0 + g < nh) load_head<HD>(row + (h0 + g) * HD, x[g]);
         }
-        store_head<HD>(p, y);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            if (h0 + g < nh) {
+#pragma unroll
+                for (int i = 0; i < E; ++i) ss[g] += x[g][i] * x[g][i];
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < G; ++g) ss[g] += __shfl_xor_sync(0xffffffffu, ss[g], o);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            if (h0 + g >= nh) continue;
+            const float r = rsqrtf(ss[g] / static_cast<float>(HD) + eps);
+            const bool is_q = h0 + g < q_heads;
+            float xs[E], y[E];
+#pragma unroll
+            for (int i = 0; i < E; ++i) xs[i] = x[g][i] * r * (is_q ? wq[i] : wk[i]);
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const float partner = __shfl_xor_sync(0xffffffffu, xs[i], 16);
+                y[i] = lo ? xs[i] * cs[i] - partner * sn[i] : xs[i] * cs[i] + partner * sn[i];
+            }
+            store_head<HD>(row + (h0 + g) * HD, y);
+        }
     }
 }
 
