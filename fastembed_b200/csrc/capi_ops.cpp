@@ -345,6 +345,20 @@ fe_status fe_rms_norm_rows(const float *x, const float *w, int32_t one_plus, flo
                 "fe_rms_norm_rows");
 }
 
+fe_status fe_rms_sandwich_bf16(const void *y, const float *w_post, float *h32, const float *w_next,
+                               int32_t one_plus, float eps, int64_t rows, int32_t dim, float *o32, void *o16,
+                               fe_stream_t stream)
+{
+    if (rows < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_sandwich_bf16: bad shape");
+    if (!rms_dim_ok(dim)) return fail(FE_ERR_UNSUPPORTED, "fe_rms_sandwich_bf16: unsupported dim");
+    if (rows == 0) return FE_OK;
+    if (!y || !w_post || !h32 || !w_next || (!o32 && !o16))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_rms_sandwich_bf16: null pointer");
+    return done(fe::launch_rms_sandwich(y, w_post, h32, w_next, one_plus != 0, eps, rows, dim, o32, o16,
+                                        reinterpret_cast<cudaStream_t>(stream), true),
+                "fe_rms_sandwich_bf16");
+}
+
 fe_status fe_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, int32_t one_plus,
                           float eps, int64_t rows, int32_t dim, float *o32, void *o16, fe_stream_t stream)
 {

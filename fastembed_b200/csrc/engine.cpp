@@ -512,19 +512,23 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
             }
         } else {
             // x <- x + rms(attn Wo^T), then the pre-FFN norm, in one row kernel
-            FE_TRY(gemm(attn, L.wo, nullptr, nullptr, y32, D, AO, FE_EPI_NONE, FE_DTYPE_F32));
+            // o_proj and down_proj are written in bf16 (y16, in the y32 buffer): the sandwich
+            // step normalises them before they reach the fp32 residual stream, and bf16 halves
+            // both their store and the sandwich's read
+            void *y16 = y32;
+            FE_TRY(gemm(attn, L.wo, nullptr, nullptr, y16, D, AO, FE_EPI_NONE, FE_DTYPE_BF16));
             {
                 Scope sc(e, CAT_OTHER, s);
-                FE_TRY_CUDA(fe::launch_rms_sandwich(y32, L.post_attn_norm.as<float>(), h32, L.pre_ff_norm.as<float>(),
-                                                    true, eps, T, static_cast<int>(D), nullptr, x16, s));
+                FE_TRY_CUDA(fe::launch_rms_sandwich(y16, L.post_attn_norm.as<float>(), h32, L.pre_ff_norm.as<float>(),
+                                                    true, eps, T, static_cast<int>(D), nullptr, x16, s, true));
             }
             FE_TRY(gemm(x16, L.wgu, nullptr, nullptr, ff, 2 * F, D, FE_EPI_GEGLU, FE_DTYPE_BF16));
-            FE_TRY(gemm(ff, L.wd, nullptr, nullptr, y32, D, F, FE_EPI_NONE, FE_DTYPE_F32));
+            FE_TRY(gemm(ff, L.wd, nullptr, nullptr, y16, D, F, FE_EPI_NONE, FE_DTYPE_BF16));
             {
                 Scope sc(e, CAT_OTHER, s);
-                FE_TRY_CUDA(fe::launch_rms_sandwich(y32, L.post_ff_norm.as<float>(), h32, next_norm, true, eps, T,
+                FE_TRY_CUDA(fe::launch_rms_sandwich(y16, L.post_ff_norm.as<float>(), h32, next_norm, true, eps, T,
                                                     static_cast<int>(D), last ? fin : nullptr, last ? nullptr : x16,
-                                                    s));
+                                                    s, true));
             }
         }
     }

@@ -84,8 +84,9 @@ cudaError_t launch_embed_scale(const int32_t *ids, int64_t total, const float *w
                                float *h32, cudaStream_t s);
 cudaError_t launch_rms_norm_rows(const float *x, const float *w, bool one_plus, float eps, int64_t rows, int dim,
                                  float *o32, void *o16, cudaStream_t s);
-cudaError_t launch_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, bool one_plus,
-                                float eps, int64_t rows, int dim, float *o32, void *o16, cudaStream_t s);
+cudaError_t launch_rms_sandwich(const void *y, const float *w_post, float *h32, const float *w_next, bool one_plus,
+                                float eps, int64_t rows, int dim, float *o32, void *o16, cudaStream_t s,
+                                bool y_bf16 = false);
 cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t total, int q_heads, int kv_heads,
                                 int head_dim, const float *q_w, const float *k_w, bool one_plus, float eps, float theta,
                                 cudaStream_t s);

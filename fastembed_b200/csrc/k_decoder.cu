@@ -116,9 +116,10 @@ __global__ void __launch_bounds__(256)
 
 // Sandwich norm step: h32 += RMSNorm(y; w_post), then out = RMSNorm(h32; w_next) as fp32
 // and / or bf16 (the post-attention / post-FFN norms of Gemma3 followed by the next pre-norm).
-template <int VPT>
+// YT: the type of y (float, or __nv_bfloat16 for a projection written in bf16).
+template <int VPT, class YT>
 __global__ void __launch_bounds__(256)
-    rms_sandwich(const float *__restrict__ y, const float *__restrict__ w_post, float *__restrict__ h32,
+    rms_sandwich(const YT *__restrict__ y, const float *__restrict__ w_post, float *__restrict__ h32,
                  const float *__restrict__ w_next, int one_plus, float eps, int64_t rows, float *__restrict__ o32,
                  __nv_bfloat16 *__restrict__ o16)
 {
@@ -128,7 +129,15 @@ __global__ void __launch_bounds__(256)
     if (r >= rows) return;
     float4 v[VPT];
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) v[i] = *reinterpret_cast<const float4 *>(y + r * dim + (i * 32 + lane) * 4);
+    for (int i = 0; i < VPT; ++i) {
+        if constexpr (sizeof(YT) == 4) {
+            v[i] = *reinterpret_cast<const float4 *>(y + r * dim + (i * 32 + lane) * 4);
+        } else {
+            const uint2 u = *reinterpret_cast<const uint2 *>(y + r * dim + (i * 32 + lane) * 4);
+            const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+            v[i] = make_float4(a.x, a.y, b.x, b.y);
+        }
+    }
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) s += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
@@ -251,6 +260,18 @@ __global__ void __launch_bounds__(256)
 
 }  // namespace
 
+#define FE_ROW_DISPATCH2(KERNEL, T2, DIM, ...)                                                        \
+    switch (DIM) {                                                                                    \
+    case 256: KERNEL<2, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
+    case 384: KERNEL<3, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
+    case 512: KERNEL<4, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
+    case 768: KERNEL<6, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
+    case 1024: KERNEL<8, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                \
+    case 1536: KERNEL<12, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                               \
+    case 2048: KERNEL<16, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                               \
+    default: return cudaErrorInvalidValue;                                                            \
+    }
+
 #define FE_ROW_DISPATCH(KERNEL, DIM, ...)                                                              \
     switch (DIM) {                                                                                    \
     case 256: KERNEL<2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                     \
@@ -283,16 +304,24 @@ cudaError_t launch_rms_norm_rows(const float *x, const float *w, bool one_plus, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, bool one_plus,
-                                float eps, int64_t rows, int dim, float *o32, void *o16, cudaStream_t s)
+cudaError_t launch_rms_sandwich(const void *y, const float *w_post, float *h32, const float *w_next, bool one_plus,
+                                float eps, int64_t rows, int dim, float *o32, void *o16, cudaStream_t s, bool y_bf16)
 {
     if (rows == 0) return cudaSuccess;
     const unsigned grid = grid_rows(rows, 8);
     auto *b16 = static_cast<__nv_bfloat16 *>(o16);
-    FE_ROW_DISPATCH(rms_sandwich, dim, y, w_post, h32, w_next, one_plus ? 1 : 0, eps, rows, o32, b16)
+    if (y_bf16) {
+        const auto *yb = static_cast<const __nv_bfloat16 *>(y);
+        FE_ROW_DISPATCH2(rms_sandwich, __nv_bfloat16, dim, yb, w_post, h32, w_next, one_plus ? 1 : 0, eps, rows, o32,
+                         b16)
+    } else {
+        const auto *yf = static_cast<const float *>(y);
+        FE_ROW_DISPATCH2(rms_sandwich, float, dim, yf, w_post, h32, w_next, one_plus ? 1 : 0, eps, rows, o32, b16)
+    }
     return cudaGetLastError();
 }
 #undef FE_ROW_DISPATCH
+#undef FE_ROW_DISPATCH2
 
 cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t total, int q_heads, int kv_heads,
                                 int head_dim, const float *q_w, const float *k_w, bool one_plus, float eps, float theta,

@@ -199,10 +199,10 @@ def rms_sandwich(y, w_post, h32, w_next, eps, one_plus=True):
     """h32 += RMSNorm(y; w_post) in place; returns (RMSNorm(h32; w_next) fp32, bf16)."""
     _cuda(y, w_post, h32, w_next)
     rows, D = y.shape
-    o32 = torch.empty_like(y)
+    o32 = torch.empty(rows, D, dtype=torch.float32, device=y.device)
     o16 = torch.empty(rows, D, dtype=torch.bfloat16, device=y.device)
-    call("fe_rms_sandwich", _p(y), _p(w_post), _p(h32), _p(w_next), 1 if one_plus else 0, eps, rows, D, _p(o32),
-         _p(o16), _s(y))
+    fn = "fe_rms_sandwich_bf16" if y.dtype == torch.bfloat16 else "fe_rms_sandwich"
+    call(fn, _p(y), _p(w_post), _p(h32), _p(w_next), 1 if one_plus else 0, eps, rows, D, _p(o32), _p(o16), _s(y))
     return o32, o16
 
 

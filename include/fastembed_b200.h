@@ -219,6 +219,11 @@ fe_status fe_embed_scale(const int32_t *ids, int64_t total_tokens, const float *
 fe_status fe_rms_norm_rows(const float *x, const float *w, int32_t one_plus, float eps, int64_t rows, int32_t dim,
                            float *o32, void *o16, fe_stream_t stream);
 /* h32 += RMSNorm(y; w_post), then out = RMSNorm(h32; w_next) as fp32 and / or bf16. */
+/* fe_rms_sandwich with y in bf16 (a projection written in bf16, as the Gemma3-shaped
+ * engine writes o_proj and down_proj): same arithmetic in fp32 after widening y. */
+fe_status fe_rms_sandwich_bf16(const void *y, const float *w_post, float *h32, const float *w_next,
+                               int32_t one_plus, float eps, int64_t rows, int32_t dim, float *o32, void *o16,
+                               fe_stream_t stream);
 fe_status fe_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, int32_t one_plus,
                           float eps, int64_t rows, int32_t dim, float *o32, void *o16, fe_stream_t stream);
 /* In place on qkv [total, (q_heads + 2*kv_heads)*head_dim] bf16: per-head RMSNorm of the

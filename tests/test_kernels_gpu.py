@@ -490,6 +490,14 @@ def test_rms_rows_and_sandwich(cuda_dev, D, one_plus):
     assert float((h - h_ref).abs().max()) < 1e-4
     assert float((s32 - _rms_ref(h_ref, w2, 1e-6, one_plus)).abs().max()) < 1e-4
     assert torch.equal(s16, s32.to(torch.bfloat16))
+    # y in bf16 (fe_rms_sandwich_bf16): the same step on the widened values
+    y16 = y.to(torch.bfloat16)
+    h2 = torch.randn(517, D, device=cuda_dev, generator=g)
+    h2_ref = h2 + _rms_ref(y16.float(), w, 1e-6, one_plus)
+    t32, t16 = ops.rms_sandwich(y16, w, h2, w2, 1e-6, one_plus)
+    assert float((h2 - h2_ref).abs().max()) < 1e-4
+    assert float((t32 - _rms_ref(h2_ref, w2, 1e-6, one_plus)).abs().max()) < 1e-4
+    assert torch.equal(t16, t32.to(torch.bfloat16))
 
 
 def _rope_ref(x, pos, theta):
