@@ -98,6 +98,9 @@ cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int ba
 // h = LayerNorm(x [+ res]); res may be null, h32 may alias res.
 cudaError_t launch_layernorm_dual(const float *x, const float *res, const float *g, const float *b,
                                   float *h32, void *h16, int64_t rows, int dim, float eps, cudaStream_t s);
+// The same with x in bf16 (a projection written in bf16).
+cudaError_t launch_layernorm_dual_bf16in(const void *x, const float *res, const float *g, const float *b, float *h32,
+                                         void *h16, int64_t rows, int dim, float eps, cudaStream_t s);
 cudaError_t launch_pool_l2(const float *h, const int32_t *cu, int batch, int dim, int mode,
                            float *out, cudaStream_t s);
 cudaError_t launch_f32_to_bf16(const float *x, void *y, int64_t count, cudaStream_t s);

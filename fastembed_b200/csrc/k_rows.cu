@@ -114,19 +114,27 @@ __global__ void __launch_bounds__(256)
 // formed here (y already holds x W^T + b), the order of the reference's residual add
 // (src/sentence_transformers_impl.cpp:255-263, :429-436).  h32 may alias res: every
 // element is read before the thread that owns it writes it.
-template <int VPT>
+template <int VPT, class IT = float>
 __global__ void __launch_bounds__(256)
-    ln_dual(const float *__restrict__ in, const float *res, const float *__restrict__ g, const float *__restrict__ b,
+    ln_dual(const IT *__restrict__ in, const float *res, const float *__restrict__ g, const float *__restrict__ b,
             float *h32, __nv_bfloat16 *__restrict__ h16, int64_t rows, float eps)
 {
     constexpr int dim = 128 * VPT;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
-    const float *src = in + r * dim;
+    const IT *src = in + r * dim;
     float4 x[VPT];
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) x[i] = *reinterpret_cast<const float4 *>(src + (i * 32 + lane) * 4);
+    for (int i = 0; i < VPT; ++i) {
+        if constexpr (sizeof(IT) == 4) {
+            x[i] = *reinterpret_cast<const float4 *>(src + (i * 32 + lane) * 4);
+        } else {  // a projection written in bf16, widened
+            const uint2 u = *reinterpret_cast<const uint2 *>(src + (i * 32 + lane) * 4);
+            const float2 p = unpack_bf16x2(u.x), q = unpack_bf16x2(u.y);
+            x[i] = make_float4(p.x, p.y, q.x, q.y);
+        }
+    }
     if (res) {
         const float *rr = res + r * dim;
 #pragma unroll
@@ -290,6 +298,23 @@ cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int ba
     case 128 * V: embed_ln<V><<<grid, 256, 0, s>>>(ids, cu, batch, total, word, pos, type, g, b, vocab, max_pos, pad_id, eps, h32, o16, st); break;
         FE_EMB(2) FE_EMB(3) FE_EMB(4) FE_EMB(6) FE_EMB(8) FE_EMB(12) FE_EMB(16)
 #undef FE_EMB
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_dual_bf16in(const void *x, const float *res, const float *g, const float *b, float *h32,
+                                         void *h16, int64_t rows, int dim, float eps, cudaStream_t s)
+{
+    if (rows == 0) return cudaSuccess;
+    auto *o16 = static_cast<__nv_bfloat16 *>(h16);
+    const auto *xb = static_cast<const __nv_bfloat16 *>(x);
+    const unsigned grid = grid_for(rows, 8);
+    switch (dim) {
+#define FE_LN(V) \
+    case 128 * V: ln_dual<V, __nv_bfloat16><<<grid, 256, 0, s>>>(xb, res, g, b, h32, o16, rows, eps); break;
+        FE_LN(1) FE_LN(2) FE_LN(3) FE_LN(4) FE_LN(6) FE_LN(8) FE_LN(12) FE_LN(16)
+#undef FE_LN
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
