@@ -147,6 +147,36 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x
                  : "memory");
 }
 
+// L2 eviction-priority policies for the cache-hinted TMA forms below.
+__device__ __forceinline__ uint64_t l2_policy_evict_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// tma_load_2d with an L2 cache-policy hint.
+__device__ __forceinline__ void tma_load_2d_hint(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y,
+                                                 uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
+// tma_store_2d with an L2 cache-policy hint.
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap *map, const void *src, int x, int y,
+                                                  uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+            map),
+        "r"(smem_u32(src)), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
 // 3-D tiled bulk tensor load (x innermost), completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z)
 {

@@ -780,9 +780,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
         uint32_t acc_phase = 0;
         const float inv_n = 1.0f / static_cast<float>(N);
         auto warp_row0 = [&](int t) { return (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + q * 32; };
+        // The residual is read once and the outputs written once: evict-first in L2, so that
+        // they do not displace the x row blocks the other column tiles of a row group read.
+        const uint64_t stream_policy = l2_policy_evict_first();
         auto load_res = [&](int b, int col, int row) {  // lane 0
             mbar_arrive_expect_tx(&rbar[b], 4096);
-            tma_load_2d(wb + b * 4096, &tm_h, &rbar[b], col, row);
+            tma_load_2d_hint(wb + b * 4096, &tm_h, &rbar[b], col, row, stream_policy);
         };
         if (lane < CH && pair < num_tiles) tma_prefetch_l2_2d(&tm_h, c0 + 32 * lane, warp_row0(pair));
         for (int tile = pair; tile < num_tiles; tile += npairs) {
@@ -1007,7 +1010,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&tm_h, fs, c0 + c * 32, row0);
+                    tma_store_2d_hint(&tm_h, fs, c0 + c * 32, row0, stream_policy);
                     bulk_commit();
                 }
                 if (write16) {
@@ -1023,7 +1026,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
                     __syncwarp();
                 }
                 if (lane == 0) {  // an empty group keeps the F / B alternation when bf16 is not written
-                    if (write16) tma_store_2d(&tm_h16, hs, c0 + c * 32, row0);
+                    if (write16) tma_store_2d_hint(&tm_h16, hs, c0 + c * 32, row0, stream_policy);
                     bulk_commit();
                 }
             }
