@@ -792,8 +792,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
             if (*abort_flag) break;
             const int row0 = warp_row0(tile);
             const int row = row0 + lane;
-            if (lane < CH && tile + npairs < num_tiles)
-                tma_prefetch_l2_2d(&tm_h, c0 + 32 * lane, warp_row0(tile + npairs));
+            // (no L2 prefetch of the next tile's residual: issued a whole round ahead, the
+            // lines were evicted before use and the residual crossed HBM twice)
             if (lane == 0) {
                 bulk_wait_read<0>();  // the previous tile's stores have read every slab
                 load_res(0, c0, row0);
