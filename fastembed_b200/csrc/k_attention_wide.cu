@@ -10,8 +10,8 @@
 // two 128-column S slots, then one or two O accumulators of head_dim columns.
 //   warp 0     TMA producer: the Q tile of a unit and the K and V tiles of each 128-key
 //              item, each as head_dim / 64 boxes of 128 rows x 128 bytes (128B swizzle);
-//              K and V advance independently, and the next unit's tiles are prefetched
-//              into L2 (measured on the Qwen3-0.6B shape, 71,550 tokens: 648 -> 557 us).
+//              K and V advance independently (measured on the Qwen3-0.6B shape, 71,550
+//              tokens, with an L2 prefetch since removed: 648 -> 557 us).
 //   warp 1     MMA issuer: S = Q K^T (K = head_dim) into an S slot; for the previous item
 //              O (+)= P V with P (bf16) read from TMEM and V an MN-major operand; the
 //              first item of a unit overwrites O.  (Issuing each PV as soon as its P is
@@ -188,22 +188,12 @@ __global__ void __launch_bounds__(kThreadsW, 1)
             // K and V tiles are loaded by two cursors over the same item sequence, each
             // as soon as its own slot is released (a K slot when the S two items back is
             // done, a V slot when that item's PV is), so no K load queues behind a V slot.
-            // A unit's Q tile is loaded when the K cursor enters the unit, and the tiles of
-            // the CTA's next unit are prefetched into L2 then.
+            // A unit's Q tile is loaded when the K cursor enters the unit.  (Prefetching the
+            // next unit's tiles into L2 then measured slower: 516 vs 502 us on the Qwen3
+            // shape, 134 vs 122 us on the Gemma one.)
             bool ok = true;
             uint32_t qn = 0, kn = 0, vn = 0;
             uint32_t q_armed = 0, q_par = 0, k_armed = 0, k_par = 0, v_armed = 0, v_par = 0;
-            auto prefetch_unit = [&](int g) {
-                if (g >= total_units) return;
-                const U w = unit(g);
-                const int kvh = w.head / group;
-                for (int b = 0; b < BOXES; ++b) tma_prefetch_l2_2d(&tm_qkv, w.head * HD + 64 * b, w.start + w.q0);
-                for (int j = 0; j < w.n_kv; ++j)
-                    for (int b = 0; b < BOXES; ++b) {
-                        tma_prefetch_l2_2d(&tm_qkv, k_col0 + kvh * HD + 64 * b, w.start + j * TK);
-                        tma_prefetch_l2_2d(&tm_qkv, v_col0 + kvh * HD + 64 * b, w.start + j * TK);
-                    }
-            };
             struct Cur {
                 int g, j;
                 U w;
@@ -219,7 +209,6 @@ __global__ void __launch_bounds__(kThreadsW, 1)
             Cur kc, vc;
             start_at(kc, blockIdx.x);
             start_at(vc, blockIdx.x);
-            prefetch_unit(blockIdx.x);
             uint64_t t_last = globaltimer_ns();
             for (uint32_t i = 0; ok && !*abort_flag; ++i) {
                 const bool k_more = kc.g < total_units, v_more = vc.g < total_units;
@@ -240,7 +229,6 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                             q_armed |= 1u << qs;
                             q_par = (q_par & ~(1u << qs)) | (((qn / QS) & 1) << qs);
                             ++qn;
-                            prefetch_unit(kc.g + static_cast<int>(gridDim.x));
                         }
                         mbar_arrive_expect_tx(&k_full[ks], C::TILE);
                         for (int b = 0; b < BOXES; ++b)
