@@ -122,6 +122,37 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
     }
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// A kernel launched by launch_k() may start (its CTAs become resident and run their
+// set-up) while the previous kernel in its stream is still running.  grid_dep_wait()
+// blocks until that kernel has completed and its memory is visible: every CTA calls it
+// before its first access to a buffer that another kernel reads or writes, and before
+// allocating TMEM.  grid_dep_launch() lets the next kernel start launching; a CTA calls
+// it after its own TMEM allocation, so a successor waiting on the same SM never holds
+// columns that this kernel still needs.  Both are no-ops for a plain launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches a kernel that calls grid_dep_wait(), with programmatic stream serialisation
+// when pdl_enabled().  Arguments are converted to the kernel's parameter types.
+template <typename... KArgs, typename... Args>
+__host__ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args)
+{
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
+}
+
 // ----------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map)
 {

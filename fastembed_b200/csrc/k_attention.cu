@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
     }
+    grid_dep_wait();
     if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem = *tmem_slot;
     const unsigned total_units = static_cast<unsigned>(upre[batch]);
 
@@ -568,11 +570,9 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
         const int64_t units_bound = static_cast<int64_t>(nb) * ((max_len + TQ - 1) / TQ) * heads;
         const int grid = units_bound < ctas ? static_cast<int>(units_bound) : ctas;
         unsigned *sched = sched_dev + 2 * (slot++ % kSchedSlots);
-        attn_varlen_tcgen05<<<grid, kThreads, SMEM_BYTES, s>>>(tm, cu_seqlens + b0, nb, heads, sched,
-                                                               static_cast<__nv_bfloat16 *>(out), scale_log2,
-                                                               static_cast<int>(total_tokens), head_major ? 1 : 0,
-                                                               current_device_status_word());
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_k(attn_varlen_tcgen05, dim3(grid), dim3(kThreads), SMEM_BYTES, s, tm, cu_seqlens + b0,
+                                 nb, heads, sched, static_cast<__nv_bfloat16 *>(out), scale_log2,
+                                 static_cast<int>(total_tokens), head_major ? 1 : 0, current_device_status_word());
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(kThreadsW, 1)
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
     }
+    grid_dep_wait();
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
@@ -150,6 +151,7 @@ __global__ void __launch_bounds__(kThreadsW, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem = *tmem_slot;
     const int total_units = upre[batch];
 
@@ -523,9 +525,8 @@ cudaError_t launch_wide(const CUtensorMap &tm, const int32_t *cu, int batch, int
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    attn_wide_tcgen05<HD><<<grid, kThreadsW, WCfg<HD>::SMEM, s>>>(tm, cu, batch, q_heads, kv_heads, causal,
-                                                                   scale_log2, out, current_device_status_word());
-    return cudaGetLastError();
+    return launch_k(attn_wide_tcgen05<HD>, dim3(grid), dim3(kThreadsW), WCfg<HD>::SMEM, s, tm, cu, batch, q_heads,
+                    kv_heads, causal, scale_log2, out, current_device_status_word());
 }
 
 }  // namespace

@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(256)
     constexpr int dim = 128 * VPT;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
     if (t >= total) return;
     const int id = ids[t];
     float *o = h32 + t * dim;
@@ -107,6 +109,8 @@ __global__ void __launch_bounds__(256)
     constexpr int dim = 128 * VPT;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
     if (r >= rows) return;
     float4 v[VPT];
 #pragma unroll
@@ -126,6 +130,8 @@ __global__ void __launch_bounds__(256)
     constexpr int dim = 128 * VPT;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
     if (r >= rows) return;
     float4 v[VPT];
 #pragma unroll
@@ -200,6 +206,8 @@ __global__ void __launch_bounds__(256)
     constexpr int E = HD / 32;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
     if (t >= total) return;
     const int pos = static_cast<int>(t - cu[sentence_of(cu, batch, t)]);
     float cs[E], sn[E], wq[E], wk[E];
@@ -261,27 +269,35 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 #define FE_ROW_DISPATCH2(KERNEL, T2, DIM, ...)                                                        \
-    switch (DIM) {                                                                                    \
-    case 256: KERNEL<2, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
-    case 384: KERNEL<3, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
-    case 512: KERNEL<4, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
-    case 768: KERNEL<6, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                 \
-    case 1024: KERNEL<8, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                \
-    case 1536: KERNEL<12, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                               \
-    case 2048: KERNEL<16, T2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                               \
-    default: return cudaErrorInvalidValue;                                                            \
+    {                                                                                                 \
+        cudaError_t fe_e_ = cudaSuccess;                                                              \
+        switch (DIM) {                                                                                \
+        case 256: fe_e_ = launch_k(KERNEL<2, T2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 384: fe_e_ = launch_k(KERNEL<3, T2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 512: fe_e_ = launch_k(KERNEL<4, T2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 768: fe_e_ = launch_k(KERNEL<6, T2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 1024: fe_e_ = launch_k(KERNEL<8, T2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;  \
+        case 1536: fe_e_ = launch_k(KERNEL<12, T2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 2048: fe_e_ = launch_k(KERNEL<16, T2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break; \
+        default: return cudaErrorInvalidValue;                                                        \
+        }                                                                                             \
+        if (fe_e_ != cudaSuccess) return fe_e_;                                                       \
     }
 
-#define FE_ROW_DISPATCH(KERNEL, DIM, ...)                                                              \
-    switch (DIM) {                                                                                    \
-    case 256: KERNEL<2><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                     \
-    case 384: KERNEL<3><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                     \
-    case 512: KERNEL<4><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                     \
-    case 768: KERNEL<6><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                     \
-    case 1024: KERNEL<8><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                    \
-    case 1536: KERNEL<12><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                   \
-    case 2048: KERNEL<16><<<grid, 256, 0, s>>>(__VA_ARGS__); break;                                   \
-    default: return cudaErrorInvalidValue;                                                            \
+#define FE_ROW_DISPATCH(KERNEL, DIM, ...)                                                         \
+    {                                                                                             \
+        cudaError_t fe_e_ = cudaSuccess;                                                          \
+        switch (DIM) {                                                                            \
+        case 256: fe_e_ = launch_k(KERNEL<2>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 384: fe_e_ = launch_k(KERNEL<3>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 512: fe_e_ = launch_k(KERNEL<4>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 768: fe_e_ = launch_k(KERNEL<6>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;   \
+        case 1024: fe_e_ = launch_k(KERNEL<8>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break;  \
+        case 1536: fe_e_ = launch_k(KERNEL<12>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break; \
+        case 2048: fe_e_ = launch_k(KERNEL<16>, dim3(grid), dim3(256), 0, s, __VA_ARGS__); break; \
+        default: return cudaErrorInvalidValue;                                                    \
+        }                                                                                         \
+        if (fe_e_ != cudaSuccess) return fe_e_;                                                   \
     }
 
 cudaError_t launch_embed_scale(const int32_t *ids, int64_t total, const float *word, int vocab, int dim, float scale,
@@ -332,14 +348,12 @@ cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t
     auto *p = static_cast<__nv_bfloat16 *>(qkv);
     const float lt = log2f(theta);
     if (head_dim == 128)
-        qk_norm_rope<128><<<grid, 256, 0, s>>>(p, cu, batch, total, q_heads, kv_heads, q_w, k_w, one_plus ? 1 : 0, eps,
-                                               lt);
-    else if (head_dim == 256)
-        qk_norm_rope<256><<<grid, 256, 0, s>>>(p, cu, batch, total, q_heads, kv_heads, q_w, k_w, one_plus ? 1 : 0, eps,
-                                               lt);
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+        return launch_k(qk_norm_rope<128>, dim3(grid), dim3(256), 0, s, p, cu, batch, total, q_heads, kv_heads, q_w, k_w,
+                        one_plus ? 1 : 0, eps, lt);
+    if (head_dim == 256)
+        return launch_k(qk_norm_rope<256>, dim3(grid), dim3(256), 0, s, p, cu, batch, total, q_heads, kv_heads, q_w, k_w,
+                        one_plus ? 1 : 0, eps, lt);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace fe

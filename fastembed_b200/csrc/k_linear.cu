@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_w);
         tma_prefetch_desc(&tm_y);
     }
+    grid_dep_wait();
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
@@ -252,6 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
@@ -542,6 +544,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
         tma_prefetch_desc(&tm_w);
         tma_prefetch_desc(&tm_y);
     }
+    grid_dep_wait();
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, P_TMEM_COLS);
         tmem_relinquish_pair();
@@ -550,6 +553,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
     __syncthreads();
     cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
@@ -737,6 +741,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
         tma_prefetch_desc(&tm_h);
         if (write16) tma_prefetch_desc(&tm_h16);
     }
+    grid_dep_wait();
     for (int i = threadIdx.x; i < 3 * P_BN; i += blockDim.x) {
         const float *src = i < P_BN ? p.bias : (i < 2 * P_BN ? p.gamma : p.beta);
         vec[i] = src[n0 + (i % P_BN)];
@@ -749,6 +754,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
     __syncthreads();
     cluster_sync();
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
@@ -1079,8 +1085,8 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
     int pairs = current_sm_count() / 2;
     if (pairs > tiles) pairs = tiles;
     if (pairs < 1) pairs = 1;
-    kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM, s>>>(tx, tw, ty, M, N, K, bias, residual, epi, status);
-    return cudaGetLastError();
+    return launch_k(kern, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, s, tx, tw, ty, M, N, K, bias, residual,
+                    epi, status);
 }
 
 // Pairs of linear_ln_tcgen05_pair<Cfg> that can be resident at once on the current
@@ -1126,9 +1132,8 @@ cudaError_t launch(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorM
     int grid = current_sm_count();
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
-    linear_tcgen05<BN, OUT_BF16><<<grid, kThreads, C::SMEM_BYTES, s>>>(tx, tw, ty, M, N, K, bias,
-                                                                       residual, epi, status);
-    return cudaGetLastError();
+    return launch_k(linear_tcgen05<BN, OUT_BF16>, dim3(grid), dim3(kThreads), C::SMEM_BYTES, s, tx, tw, ty, M, N, K,
+                    bias, residual, epi, status);
 }
 
 // The 2-CTA kernel is the default for large M; FE_LINEAR_PAIR=0 selects the 1-CTA
@@ -1325,8 +1330,8 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
     const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
     const int w16 = h16 != nullptr;
     int *status = current_device_status_word();
-    var.kern<<<2 * pairs, var.threads, var.smem, s>>>(tx, tw, th, th16, M, N, K, p, w16, status);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(var.kern, dim3(2 * pairs), dim3(var.threads), var.smem, s, tx, tw, th, th16, M, N, K, p,
+                             w16, status);
     if (e != cudaSuccess) return e;
     if (order) {
         if (!g_ln_last[dev]) {

@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(256)
     constexpr int dim = 128 * VPT;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
     if (t >= total) return;
     // sentence of token t: last s with cu[s] <= t
     int lo = 0, hi = batch - 1;
@@ -122,6 +124,8 @@ __global__ void __launch_bounds__(256)
     constexpr int dim = 128 * VPT;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
     if (r >= rows) return;
     const IT *src = in + r * dim;
     float4 x[VPT];
@@ -244,6 +248,8 @@ __global__ void __launch_bounds__(256)
 {
     const int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
     if (s >= batch) return;
     const int start = cu[s], len = cu[s + 1] - cu[s];
     float *o = out + static_cast<int64_t>(s) * dim;
@@ -294,13 +300,14 @@ cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int ba
     int *st = current_device_status_word();
     const unsigned grid = grid_for(total, 8);
     switch (dim) {
-#define FE_EMB(V) \
-    case 128 * V: embed_ln<V><<<grid, 256, 0, s>>>(ids, cu, batch, total, word, pos, type, g, b, vocab, max_pos, pad_id, eps, h32, o16, st); break;
+#define FE_EMB(V)                                                                                                \
+    case 128 * V:                                                                                                \
+        return launch_k(embed_ln<V>, dim3(grid), dim3(256), 0, s, ids, cu, batch, total, word, pos, type, g, b, vocab, \
+                        max_pos, pad_id, eps, h32, o16, st);
         FE_EMB(2) FE_EMB(3) FE_EMB(4) FE_EMB(6) FE_EMB(8) FE_EMB(12) FE_EMB(16)
 #undef FE_EMB
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_layernorm_dual_bf16in(const void *x, const float *res, const float *g, const float *b, float *h32,
@@ -312,12 +319,11 @@ cudaError_t launch_layernorm_dual_bf16in(const void *x, const float *res, const 
     const unsigned grid = grid_for(rows, 8);
     switch (dim) {
 #define FE_LN(V) \
-    case 128 * V: ln_dual<V, __nv_bfloat16><<<grid, 256, 0, s>>>(xb, res, g, b, h32, o16, rows, eps); break;
+    case 128 * V: return launch_k(ln_dual<V, __nv_bfloat16>, dim3(grid), dim3(256), 0, s, xb, res, g, b, h32, o16, rows, eps);
         FE_LN(1) FE_LN(2) FE_LN(3) FE_LN(4) FE_LN(6) FE_LN(8) FE_LN(12) FE_LN(16)
 #undef FE_LN
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_layernorm_dual(const float *x, const float *res, const float *g, const float *b, float *h32,
@@ -328,7 +334,7 @@ cudaError_t launch_layernorm_dual(const float *x, const float *res, const float 
     const unsigned grid = grid_for(rows, 8);
     switch (dim) {
 #define FE_LN(V) \
-    case 128 * V: ln_dual<V><<<grid, 256, 0, s>>>(x, res, g, b, h32, o16, rows, eps); break;
+    case 128 * V: return launch_k(ln_dual<V>, dim3(grid), dim3(256), 0, s, x, res, g, b, h32, o16, rows, eps);
         FE_LN(1) FE_LN(2) FE_LN(3) FE_LN(4) FE_LN(6) FE_LN(8) FE_LN(12) FE_LN(16)
 #undef FE_LN
         default:
@@ -365,8 +371,7 @@ cudaError_t launch_pool_l2(const float *h, const int32_t *cu, int batch, int dim
                            cudaStream_t s)
 {
     if (batch == 0) return cudaSuccess;
-    pool_l2<<<grid_for(batch, 8), 256, 0, s>>>(h, cu, batch, dim, mode, out);
-    return cudaGetLastError();
+    return launch_k(pool_l2, dim3(grid_for(batch, 8)), dim3(256), 0, s, h, cu, batch, dim, mode, out);
 }
 
 cudaError_t launch_f32_to_bf16(const float *x, void *y, int64_t count, cudaStream_t s)

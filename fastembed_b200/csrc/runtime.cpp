@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -77,6 +78,15 @@ int current_sm_count()
         g_sm_count[dev] = n > 0 ? n : 148;
     }
     return g_sm_count[dev];
+}
+
+bool pdl_enabled()
+{
+    static const bool on = [] {
+        const char *v = getenv("FE_PDL");
+        return v && v[0] == '1';
+    }();
+    return on;
 }
 
 namespace {
