@@ -100,6 +100,7 @@ _SIGS = {
     "fe_engine_set_profiling": ([vp, C.c_int], C.c_int),
     "fe_engine_get_stats": ([vp, C.POINTER(EngineStats)], C.c_int),
     "fe_plan_shards": ([C.POINTER(EncoderConfig), vp, i32, i32, vp], C.c_int),
+    "fe_plan_shards_costs": ([vp, i32, i32, vp], C.c_int),
     "fe_pack_batch": ([vp, vp, i32, i32, vp, vp], C.c_int),
 }
 

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <string>
 #include <vector>
 
@@ -400,6 +401,28 @@ fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, i
 }
 
 // ------------------------------------------------------------ host-only helpers
+}  // extern "C"
+
+namespace {
+// Greedy prefix cuts: cut r goes to the sentence boundary nearest total * r / parts
+// (ties to the earlier boundary), never before the previous cut.
+void cut_prefix(const std::vector<double> &prefix, int32_t batch, int32_t parts, int32_t *cuts)
+{
+    const double total = prefix[batch];
+    int32_t lo = 0;
+    for (int32_t r = 1; r < parts; ++r) {
+        const double target = total * r / parts;
+        int32_t i = static_cast<int32_t>(std::lower_bound(prefix.begin(), prefix.end(), target) - prefix.begin());
+        if (i > 0 && (i > batch || target - prefix[i - 1] <= prefix[i] - target)) --i;
+        i = std::min(std::max(i, lo), batch);
+        cuts[r - 1] = i;
+        lo = i;
+    }
+}
+}  // namespace
+
+extern "C" {
+
 fe_status fe_plan_shards(const fe_encoder_config *cfg, const int32_t *sorted_lengths, int32_t batch, int32_t parts,
                          int32_t *cuts)
 {
@@ -413,16 +436,21 @@ fe_status fe_plan_shards(const fe_encoder_config *cfg, const int32_t *sorted_len
             return fail(FE_ERR_INVALID_ARGUMENT, "fe_plan_shards: lengths must be sorted in descending order");
         prefix[i + 1] = prefix[i] + cfg->layers * (2.0 * L * (4 * D * D + 2 * D * F) + 4.0 * L * L * D);
     }
-    const double total = prefix[batch];
-    int32_t lo = 0;
-    for (int32_t r = 1; r < parts; ++r) {
-        const double target = total * r / parts;
-        int32_t i = static_cast<int32_t>(std::lower_bound(prefix.begin(), prefix.end(), target) - prefix.begin());
-        if (i > 0 && (i > batch || target - prefix[i - 1] <= prefix[i] - target)) --i;
-        i = std::min(std::max(i, lo), batch);
-        cuts[r - 1] = i;
-        lo = i;
+    cut_prefix(prefix, batch, parts, cuts);
+    return FE_OK;
+}
+
+fe_status fe_plan_shards_costs(const double *costs, int32_t batch, int32_t parts, int32_t *cuts)
+{
+    if (batch < 0 || parts < 1 || (batch && !costs) || (parts > 1 && !cuts))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_plan_shards_costs: bad arguments");
+    std::vector<double> prefix(static_cast<size_t>(batch) + 1, 0.0);
+    for (int32_t i = 0; i < batch; ++i) {
+        if (!std::isfinite(costs[i]) || costs[i] < 0)
+            return fail(FE_ERR_INVALID_ARGUMENT, "fe_plan_shards_costs: costs must be finite and non-negative");
+        prefix[i + 1] = prefix[i] + costs[i];
     }
+    cut_prefix(prefix, batch, parts, cuts);
     return FE_OK;
 }
 

@@ -325,10 +325,20 @@ def pack(ids: np.ndarray, lengths: np.ndarray):
 
 
 def plan_shards(shape, sorted_lengths: np.ndarray, parts: int) -> list[int]:
-    cfg = capi.EncoderConfig(shape.vocab, shape.hidden, shape.layers, shape.heads, shape.intermediate,
-                             shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], 0)
+    """Contiguous FLOP-balanced cut points of a length-sorted batch (fe_plan_shards for the
+    BERT family; fe_plan_shards_costs over the shape's own per-sentence FLOPs for the
+    Qwen3 / Gemma3 shapes)."""
     L = np.ascontiguousarray(sorted_lengths, dtype=np.int32)
     cuts = np.zeros(max(parts - 1, 1), np.int32)
-    call("fe_plan_shards", C.byref(cfg), L.ctypes.data_as(C.c_void_p), L.size, parts,
-         cuts.ctypes.data_as(C.c_void_p))
+    if hasattr(shape, "family"):
+        if L.size > 1 and np.any(L[1:] > L[:-1]):
+            raise ValueError("plan_shards: lengths must be sorted in descending order")
+        costs = np.array([shape.flops_per_sentence(int(x)) for x in L], np.float64)
+        call("fe_plan_shards_costs", costs.ctypes.data_as(C.c_void_p), L.size, parts,
+             cuts.ctypes.data_as(C.c_void_p))
+    else:
+        cfg = capi.EncoderConfig(shape.vocab, shape.hidden, shape.layers, shape.heads, shape.intermediate,
+                                 shape.max_pos, shape.type_vocab, shape.eps, ACT[shape.act], 0)
+        call("fe_plan_shards", C.byref(cfg), L.ctypes.data_as(C.c_void_p), L.size, parts,
+             cuts.ctypes.data_as(C.c_void_p))
     return [int(c) for c in cuts[:parts - 1]]

@@ -341,6 +341,10 @@ fe_status fe_engine_get_stats(const fe_engine *e, fe_engine_stats *stats);
  * algorithmic FLOPs (parts-1 cuts written to `cuts`).  Host only; no GPU needed. */
 fe_status fe_plan_shards(const fe_encoder_config *cfg, const int32_t *sorted_lengths,
                          int32_t batch, int32_t parts, int32_t *cuts);
+/* The same cut rule over explicit per-sentence costs (any model family, e.g. the
+ * Qwen3 / Gemma3 shapes' FLOPs): parts-1 contiguous cut points giving slices of
+ * near-equal total cost.  Costs must be finite and non-negative.  Host only. */
+fe_status fe_plan_shards_costs(const double *costs, int32_t batch, int32_t parts, int32_t *cuts);
 /* Packs right-padded host ids [batch, stride] with lengths into ids_packed
  * [sum(lengths)] and cu_seqlens [batch+1].  Host only. */
 fe_status fe_pack_batch(const int32_t *ids, const int32_t *lengths, int32_t batch,

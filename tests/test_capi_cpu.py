@@ -24,7 +24,7 @@ def test_header_declares_the_op_and_engine_api():
     for must in ("fe_linear_bf16", "fe_attention_varlen_bf16", "fe_embed_layernorm", "fe_layernorm_dual",
                  "fe_linear_layernorm_bf16",
                  "fe_pool_l2", "fe_sgemm_nt", "fe_mha_f32", "fe_engine_create", "fe_engine_encode_packed",
-                 "fe_engine_encode_host", "fe_plan_shards"):
+                 "fe_engine_encode_host", "fe_plan_shards", "fe_plan_shards_costs"):
         assert must in names
 
 
@@ -114,3 +114,37 @@ def test_plan_shards_matches_python_and_balances(fe_lib, parts):
     assert max(work) / (sum(work) / parts) < 1.02  # within 2% of a perfect split
     with pytest.raises(Exception):
         ops.plan_shards(shape, L[::-1].copy(), parts)  # ascending order is rejected
+
+
+@pytest.mark.parametrize("name", ["qwen3-0.6b", "gemma-300m"])
+@pytest.mark.parametrize("parts", [2, 4, 8])
+def test_plan_shards_rms_shapes(fe_lib, name, parts):
+    """The Qwen3 / Gemma3 shapes split by their own per-sentence FLOPs
+    (fe_plan_shards_costs), as bench.py does for torchrun ranks."""
+    from fastembed_b200 import ops, workload as W
+    shape = W.RMS_SHAPES[name]
+    L = np.sort(W.sample_rms_lengths(shape, batch=shape.batch * parts))[::-1].copy()
+    cuts = ops.plan_shards(shape, L, parts)
+    assert cuts == W.balanced_cuts(shape, L, parts)
+    bounds = [0] + cuts + [L.size]
+    assert all(a < b for a, b in zip(bounds, bounds[1:]))
+    work = [sum(shape.flops_per_sentence(int(x)) for x in L[a:b]) for a, b in zip(bounds, bounds[1:])]
+    assert max(work) / (sum(work) / parts) < 1.02
+
+
+def test_plan_shards_costs_matches_the_bert_planner(fe_lib):
+    import ctypes as C
+    from fastembed_b200 import capi, ops, workload as W
+    shape = W.SHAPES["bge-base"]
+    L = np.sort(W.sample_lengths(shape, batch=500, seed=3))[::-1].copy()
+    costs = np.array([shape.flops_per_sentence(int(x)) for x in L], np.float64)
+    for parts in (1, 3, 8):
+        cuts = np.zeros(max(parts - 1, 1), np.int32)
+        capi.call("fe_plan_shards_costs", costs.ctypes.data_as(C.c_void_p), L.size, parts,
+                  cuts.ctypes.data_as(C.c_void_p))
+        assert [int(c) for c in cuts[:parts - 1]] == ops.plan_shards(shape, L, parts)
+    bad = costs.copy()
+    bad[5] = -1.0
+    with pytest.raises(Exception):
+        capi.call("fe_plan_shards_costs", bad.ctypes.data_as(C.c_void_p), L.size, 2,
+                  np.zeros(1, np.int32).ctypes.data_as(C.c_void_p))
