@@ -25,6 +25,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "coalescer.h"
 #include "fastembed_b200.h"
 #include "json_min.h"
 #include "sentence_transformers.h"
@@ -227,15 +228,25 @@ public:
         return ids;
     }
 
+    // Concurrent calls (threads sharing this object, as the reference's HTTP server does)
+    // are merged into one device batch by the coalescer; the engine's outputs do not
+    // depend on which other sentences share the batch.
     std::vector<std::vector<float>> run(const std::vector<std::vector<int32_t>> &seqs)
     {
-        std::lock_guard<std::mutex> lk(mu_);
-        const int B = static_cast<int>(seqs.size());
-        std::vector<std::vector<float>> out(B, std::vector<float>(dim()));
-        if (B == 0) return out;
         for (const auto &s : seqs)
             if (static_cast<int>(s.size()) > cfg_.max_position)
                 throw std::runtime_error("sequence longer than the position embedding table");  // (:132-136)
+        if (seqs.empty()) return {};
+        return coalescer_.submit(seqs);
+    }
+
+private:
+    // One packed pass per GPU over `seqs` (run by one thread at a time, the coalescer's leader).
+    std::vector<std::vector<float>> run_batch(const std::vector<std::vector<int32_t>> &seqs)
+    {
+        const int B = static_cast<int>(seqs.size());
+        std::vector<std::vector<float>> out(B, std::vector<float>(dim()));
+        if (B == 0) return out;
         // longest first, so that contiguous slices are balanced by fe_plan_shards
         std::vector<int> order(B);
         std::iota(order.begin(), order.end(), 0);
@@ -291,11 +302,18 @@ public:
         return out;
     }
 
-private:
     fe_encoder_config cfg_{};
     std::unique_ptr<WordPiece> tokenizer_;
     std::vector<fe_engine *> engines_;
-    std::mutex mu_;
+    fe::Coalescer<std::vector<int32_t>, std::vector<float>> coalescer_{
+        [this](const std::vector<std::vector<int32_t>> &seqs) { return run_batch(seqs); }, coalesce_limit()};
+
+    // Sentences per merged batch: FE_COALESCE_MAX (0 turns merging off), else 256 per GPU.
+    static size_t coalesce_limit()
+    {
+        if (const char *env = std::getenv("FE_COALESCE_MAX")) return static_cast<size_t>(std::strtoul(env, nullptr, 10));
+        return 256 * devices().size();
+    }
 
     static std::vector<int> devices()
     {

@@ -4,8 +4,10 @@
 //
 //   st_check <model_dir> <texts_file> <out_prefix>
 // reads one text per line and writes <out_prefix>.ids (per text: int32 count, then the
-// ids), <out_prefix>.batch (float32 [n, dim] from encode_batch) and <out_prefix>.single
-// (float32 [n, dim] from encode, one text at a time).
+// ids), <out_prefix>.batch (float32 [n, dim] from encode_batch), <out_prefix>.single
+// (float32 [n, dim] from encode, one text at a time) and <out_prefix>.concurrent (the
+// same, from eight threads calling encode on the shared object at once, as the
+// reference's HTTP server does; the calls are merged into shared device batches).
 //   st_check <model_dir> <ids_file> <out_prefix> ids
 // reads token ids in the .ids format and writes <out_prefix>.batch from encode_ids (the
 // path of models whose tokenizer this build does not include, e.g. bge-m3).
@@ -13,7 +15,9 @@
 #include <cstdio>
 #include <fstream>
 #include <iostream>
+#include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "sentence_transformers.h"
@@ -65,6 +69,25 @@ int main(int argc, char **argv)
             const std::vector<float> e = model.encode(t);
             single.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());
         }
+        std::vector<std::vector<float>> conc(texts.size());
+        std::vector<std::string> errs(8);
+        {
+            std::vector<std::thread> pool;
+            for (int t = 0; t < 8; ++t)
+                pool.emplace_back([&, t] {
+                    try {
+                        for (int rep = 0; rep < 4; ++rep)  // several rounds, so that calls overlap
+                            for (size_t i = t; i < texts.size(); i += 8) conc[i] = model.encode(texts[i]);
+                    } catch (const std::exception &ex) {
+                        errs[t] = ex.what();
+                    }
+                });
+            for (auto &th : pool) th.join();
+        }
+        for (const auto &e : errs)
+            if (!e.empty()) throw std::runtime_error("concurrent encode: " + e);
+        std::ofstream concurrent(pre + ".concurrent", std::ios::binary);
+        for (const auto &e : conc) concurrent.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());
         std::printf("dim %zu, %zu texts\n", model.get_embedding_dimension(), texts.size());
     } catch (const std::exception &ex) {
         std::fprintf(stderr, "error: %s\n", ex.what());

@@ -148,3 +148,12 @@ def test_plan_shards_costs_matches_the_bert_planner(fe_lib):
     with pytest.raises(Exception):
         capi.call("fe_plan_shards_costs", bad.ctypes.data_as(C.c_void_p), L.size, 2,
                   np.zeros(1, np.int32).ctypes.data_as(C.c_void_p))
+
+
+def test_coalescer_merges_concurrent_calls():
+    """fe::Coalescer, which merges concurrent SentenceTransformer calls into one device
+    batch (host-only: tests/cpp/coalescer_check.cpp)."""
+    here = os.path.join(ROOT, "tests", "cpp")
+    subprocess.run(["make", "-s", "-C", here, os.path.join(here, "coalescer_check")], check=True)
+    r = subprocess.run([os.path.join(here, "coalescer_check")], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr

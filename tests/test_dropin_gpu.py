@@ -74,6 +74,8 @@ def _run_model(tmp_path, dtype, env_extra=None):
     D = shape.hidden
     batch = np.fromfile(pre + ".batch", dtype=np.float32).reshape(-1, D)
     single = np.fromfile(pre + ".single", dtype=np.float32).reshape(-1, D)
+    concurrent = np.fromfile(pre + ".concurrent", dtype=np.float32).reshape(-1, D)
+    assert np.array_equal(concurrent, single)  # threads sharing the object: merged batches, same rows
     used = weights if dtype == "F32" else {k: bf16_round_trip(v) for k, v in weights.items()}
     return shape, vocab, used, ids, batch, single
 
