@@ -14,6 +14,7 @@
 #include <cctype>
 #include <cstdio>
 #include <cstdlib>
+#include <exception>
 #include <fstream>
 #include <iostream>
 #include <mutex>
@@ -228,6 +229,34 @@ public:
         return ids;
     }
 
+    // A batch's texts tokenised on host threads: contiguous chunks of at least 32 texts, at
+    // most 32 threads (WordPiece::ids only reads the vocabulary).
+    std::vector<std::vector<int32_t>> tokenize_all(const std::vector<std::string> &texts) const
+    {
+        const size_t n = texts.size();
+        std::vector<std::vector<int32_t>> seqs(n);
+        const size_t hw = std::max<size_t>(1, std::thread::hardware_concurrency());
+        const size_t workers = std::min<size_t>({hw, 32, (n + 31) / 32});
+        if (workers <= 1) {
+            for (size_t i = 0; i < n; ++i) seqs[i] = tokenize(texts[i]);
+            return seqs;
+        }
+        std::vector<std::exception_ptr> errs(workers);
+        std::vector<std::thread> pool;
+        for (size_t w = 0; w < workers; ++w)
+            pool.emplace_back([&, w] {
+                try {
+                    for (size_t i = n * w / workers; i < n * (w + 1) / workers; ++i) seqs[i] = tokenize(texts[i]);
+                } catch (...) {
+                    errs[w] = std::current_exception();
+                }
+            });
+        for (auto &t : pool) t.join();
+        for (const auto &e : errs)
+            if (e) std::rethrow_exception(e);
+        return seqs;
+    }
+
     // Concurrent calls (threads sharing this object, as the reference's HTTP server does)
     // are merged into one device batch by the coalescer; the engine's outputs do not
     // depend on which other sentences share the batch.
@@ -347,10 +376,7 @@ std::vector<float> SentenceTransformer::encode(const std::string &text)
 
 std::vector<std::vector<float>> SentenceTransformer::encode_batch(const std::vector<std::string> &texts)
 {
-    std::vector<std::vector<int32_t>> seqs;
-    seqs.reserve(texts.size());
-    for (const auto &t : texts) seqs.push_back(impl->tokenize(t));
-    return impl->run(seqs);
+    return impl->run(impl->tokenize_all(texts));
 }
 
 std::vector<std::vector<float>> SentenceTransformer::encode_ids(const std::vector<std::vector<int32_t>> &ids)

@@ -3,11 +3,14 @@
 // model-level test in tests/test_dropin_gpu.py.
 //
 //   st_check <model_dir> <texts_file> <out_prefix>
-// reads one text per line and writes <out_prefix>.ids (per text: int32 count, then the
-// ids), <out_prefix>.batch (float32 [n, dim] from encode_batch), <out_prefix>.single
-// (float32 [n, dim] from encode, one text at a time) and <out_prefix>.concurrent (the
-// same, from eight threads calling encode on the shared object at once, as the
-// reference's HTTP server does; the calls are merged into shared device batches).
+// reads one text per line and writes, as float32 [rows, dim] unless noted:
+//   <out_prefix>.ids         per text: int32 count, then the ids;
+//   <out_prefix>.batch       encode_batch of the texts;
+//   <out_prefix>.big         encode_batch of the texts repeated 40 times (tokenised on
+//                            several host threads);
+//   <out_prefix>.single      encode, one text at a time;
+//   <out_prefix>.concurrent  encode from eight threads sharing the object at once, as the
+//                            reference's HTTP server does (merged into shared device batches).
 //   st_check <model_dir> <ids_file> <out_prefix> ids
 // reads token ids in the .ids format and writes <out_prefix>.batch from encode_ids (the
 // path of models whose tokenizer this build does not include, e.g. bge-m3).
@@ -65,6 +68,13 @@ int main(int argc, char **argv)
         }
         for (const auto &e : model.encode_batch(texts))
             batch.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());
+        {
+            // a batch large enough to be tokenised on several host threads: the texts 40 times
+            std::vector<std::string> big;
+            for (int r = 0; r < 40; ++r) big.insert(big.end(), texts.begin(), texts.end());
+            std::ofstream out(pre + ".big", std::ios::binary);
+            for (const auto &e : model.encode_batch(big)) out.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());
+        }
         for (const auto &t : texts) {
             const std::vector<float> e = model.encode(t);
             single.write(reinterpret_cast<const char *>(e.data()), 4 * e.size());

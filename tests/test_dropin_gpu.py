@@ -76,6 +76,12 @@ def _run_model(tmp_path, dtype, env_extra=None):
     single = np.fromfile(pre + ".single", dtype=np.float32).reshape(-1, D)
     concurrent = np.fromfile(pre + ".concurrent", dtype=np.float32).reshape(-1, D)
     assert np.array_equal(concurrent, single)  # threads sharing the object: merged batches, same rows
+    # the texts 40 times in one batch, tokenised on several host threads: every repetition
+    # gives the same rows; against the small batch (which runs the 1-CTA GEMM and the
+    # two-launch norm instead of the 2-CTA GEMM and the fused norm) within fp32 rounding
+    big = np.fromfile(pre + ".big", dtype=np.float32).reshape(40, -1, D)
+    assert all(np.array_equal(big[0], big[r]) for r in range(1, 40))
+    assert np.abs(big[0] - batch).max() <= 1e-5
     used = weights if dtype == "F32" else {k: bf16_round_trip(v) for k, v in weights.items()}
     return shape, vocab, used, ids, batch, single
 
