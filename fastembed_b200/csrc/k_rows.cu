@@ -241,7 +241,8 @@ __global__ void __launch_bounds__(256)
     for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) y[i] = y[i] / s;
 }
 
-// Pooling + L2 (src/sentence_transformers_impl.cpp:289-341): one warp per sentence.
+// Pooling + L2 (src/sentence_transformers_impl.cpp:289-341): one warp per sentence (the CLS
+// and last-token rows; mean pooling of dims that pool_mean_l2 does not take).
 __global__ void __launch_bounds__(256)
     pool_l2(const float *__restrict__ h, const int32_t *__restrict__ cu, int batch, int dim, int mode,
             float *__restrict__ out)
@@ -277,6 +278,62 @@ __global__ void __launch_bounds__(256)
     }
     const float nrm = sqrtf(warp_sum(ss));
     for (int c = lane; c < dim; c += 32) o[c] = o[c] / nrm;
+}
+
+// Mean pooling + L2 (src/sentence_transformers_impl.cpp:289-341, the mean branch), one
+// block of W warps per sentence: warp w sums the sentence's tokens w, w + W, w + 2W, ... over
+// float4 columns (four rows in flight), the W partial sums are added in warp order through
+// shared memory ([W][dim] floats), and the mean is L2-normalised.  The summation order
+// depends only on the sentence's length, so a sentence gives the same row in any batch.
+// Needs dim % 4 == 0 and W * dim * 4 bytes of dynamic shared memory.
+template <int W>
+__global__ void __launch_bounds__(W * 32)
+    pool_mean_l2(const float *__restrict__ h, const int32_t *__restrict__ cu, int dim, float *__restrict__ out)
+{
+    extern __shared__ float part[];  // [W][dim]
+    __shared__ float red[W];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
+    const int s = blockIdx.x;
+    const int start = cu[s], len = cu[s + 1] - cu[s];
+    float *o = out + static_cast<int64_t>(s) * dim;
+    if (len <= 0) {
+        for (int c = threadIdx.x; c < dim; c += blockDim.x) o[c] = 0.f;
+        return;
+    }
+    const int d4 = dim >> 2;
+    const float4 *base = reinterpret_cast<const float4 *>(h + static_cast<int64_t>(start) * dim);
+    for (int c4 = lane; c4 < d4; c4 += 32) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int t = warp; t < len; t += W) {
+            const float4 v = __ldg(base + static_cast<int64_t>(t) * d4 + c4);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        reinterpret_cast<float4 *>(part + warp * dim)[c4] = acc;
+    }
+    __syncthreads();
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < W; ++w) a += part[w * dim + c];
+        a /= static_cast<float>(len);
+        part[c] = a;  // column c is read and written by this thread only
+        ss += a * a;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) tot += red[w];
+    const float nrm = sqrtf(tot);
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) o[c] = part[c] / nrm;
 }
 
 __global__ void f32_to_bf16(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y, int64_t n)
@@ -371,6 +428,17 @@ cudaError_t launch_pool_l2(const float *h, const int32_t *cu, int batch, int dim
                            cudaStream_t s)
 {
     if (batch == 0) return cudaSuccess;
+    if (mode == FE_POOL_MEAN && dim % 4 == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+        // one block per sentence (float4 rows: dim % 4 == 0 and h 16-byte aligned); W warps so
+        // that the [W][dim] partial sums and the W-float reduction array fit in 48 KB
+        const size_t row = static_cast<size_t>(dim) * sizeof(float), cap = 48 * 1024;
+        if (8 * row + 8 * 4 <= cap)
+            return launch_k(pool_mean_l2<8>, dim3(batch), dim3(256), 8 * row, s, h, cu, dim, out);
+        if (4 * row + 4 * 4 <= cap)
+            return launch_k(pool_mean_l2<4>, dim3(batch), dim3(128), 4 * row, s, h, cu, dim, out);
+        if (2 * row + 2 * 4 <= cap)
+            return launch_k(pool_mean_l2<2>, dim3(batch), dim3(64), 2 * row, s, h, cu, dim, out);
+    }
     return launch_k(pool_l2, dim3(grid_for(batch, 8)), dim3(256), 0, s, h, cu, batch, dim, mode, out);
 }
 

@@ -398,6 +398,37 @@ def test_pool_l2_indices(cuda_dev, mode):
         assert float((out[b] - v).abs().max()) <= tol + 1e-7
 
 
+@pytest.mark.parametrize("D", [256, 768, 1024, 1532, 1536, 2048, 4000, 6140, 6144, 770])
+def test_pool_mean_l2_shapes(cuda_dev, D):
+    """Mean pooling + L2 over the dims of each kernel form (block per sentence with 8 / 4 / 2
+    warps, and the warp-per-sentence kernel for dim % 4 != 0, an unaligned base or a dim whose
+    partial sums exceed 48 KB), with an
+    empty sentence and sentences past 256 tokens; a sentence alone gives its row of the batch
+    bit for bit.  Tolerance 1e-5 against a float64 reference of the mean."""
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(D)
+    lens = [3, 0, 300, 1, 64, 257, 17]
+    h = torch.randn(sum(lens) + 1, D, device=cuda_dev, generator=g)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    aligned = h[:-1]
+    for hh in (aligned, h.view(-1)[1:sum(lens) * D + 1].view(sum(lens), D)):  # aligned, then 4 bytes off
+        out = ops.pool_l2(hh, cu, "mean")
+        ref = hh.double()
+        starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+        for b, (s0, L) in enumerate(zip(starts, lens)):
+            if L == 0:
+                assert bool((out[b] == 0).all())
+                continue
+            v = ref[s0:s0 + L].mean(0)
+            v = v / v.norm()
+            assert float((out[b].double() - v).abs().max()) <= 1e-5, (D, b)
+        for b in ((2, 5) if hh is aligned else ()):  # the slice below is aligned: same kernel only then
+            s0, L = int(starts[b]), lens[b]
+            one = ops.pool_l2(hh[s0:s0 + L].contiguous(), torch.tensor([0, L], dtype=torch.int32, device=cuda_dev),
+                              "mean")
+            assert torch.equal(one[0], out[b])
+
+
 # ------------------------------------------------------------ fp32 op API
 def test_fp32_ops_match_oracle(cuda_dev, oracle_lib):
     from fastembed_b200 import ops
