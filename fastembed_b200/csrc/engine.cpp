@@ -102,6 +102,7 @@ struct fe_engine {
     fe_rms_encoder_config rc{};  // RMSNorm families
     std::vector<RLayer> rlayers;
     DevBuf final_norm, zero_bias, hfin;  // hfin: final-norm output [T, D] fp32 (RMSNorm families)
+    DevBuf tpos;                         // int32 [T]: each token's position in its sentence (RMSNorm families)
     DevBuf staging16;  // bf16 conversion buffer of interleaved uploads
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -401,6 +402,7 @@ fe_status ensure_activations_rms(fe_engine *e, int64_t T)
     FE_TRY_CUDA(e->y32.ensure(cap * D * 4));
     FE_TRY_CUDA(e->ff.ensure(cap * F * 2));
     FE_TRY_CUDA(e->hfin.ensure(cap * D * 4));
+    FE_TRY_CUDA(e->tpos.ensure(cap * 4));
     const size_t ws = fe::linear_layernorm_stats_bytes(cap, static_cast<int64_t>(D));
     FE_TRY_CUDA(e->ln_ws.ensure(ws));
     FE_TRY_CUDA(cudaMemset(e->ln_ws.p, 0, ws));
@@ -478,6 +480,7 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
         // Gemma3 scales the embeddings by sqrt(hidden) (rounded to fp32); Qwen3 does not
         const float escale = gemma ? static_cast<float>(std::sqrt(static_cast<double>(D))) : 1.0f;
         FE_TRY_CUDA(fe::launch_embed_scale(ids, T, e->word.as<float>(), c.vocab_size, static_cast<int>(D), escale, h32, s));
+        FE_TRY_CUDA(fe::launch_token_positions(cu, batch, e->tpos.as<int32_t>(), s));
     }
     {
         Scope sc(e, CAT_OTHER, s);
@@ -493,7 +496,7 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
             Scope sc(e, CAT_OTHER, s);
             FE_TRY_CUDA(fe::launch_qk_norm_rope(qkv, cu, batch, T, c.q_heads, c.kv_heads, static_cast<int>(hd),
                                                 L.q_norm.as<float>(), L.k_norm.as<float>(), gemma, eps,
-                                                layer_theta(c, l), s));
+                                                layer_theta(c, l), s, e->tpos.as<int32_t>()));
         }
         {
             Scope sc(e, CAT_ATTN, s);

@@ -93,9 +93,12 @@ cudaError_t launch_rms_norm_rows(const float *x, const float *w, bool one_plus, 
 cudaError_t launch_rms_sandwich(const void *y, const float *w_post, float *h32, const float *w_next, bool one_plus,
                                 float eps, int64_t rows, int dim, float *o32, void *o16, cudaStream_t s,
                                 bool y_bf16 = false);
+// pos: the positions array of launch_token_positions, or null to search cu for each token
 cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t total, int q_heads, int kv_heads,
                                 int head_dim, const float *q_w, const float *k_w, bool one_plus, float eps, float theta,
-                                cudaStream_t s);
+                                cudaStream_t s, const int32_t *pos = nullptr);
+// pos[t] = position of token t in its sentence, for the packed batch of cu [batch + 1]
+cudaError_t launch_token_positions(const int32_t *cu, int batch, int32_t *pos, cudaStream_t s);
 cudaError_t launch_embed_layernorm(const int32_t *ids, const int32_t *cu, int batch, int64_t total,
                                    const float *word, const float *pos, const float *type,
                                    const float *g, const float *b, int dim, int vocab,

@@ -197,11 +197,37 @@ __device__ __forceinline__ void store_head(__nv_bfloat16 *p, const float (&y)[HD
     }
 }
 
+// pos[t] = t - (first token of t's sentence) for the packed batch: one warp per sentence.
+// Built once per forward pass; every layer's qk_norm_rope then reads a token's position
+// instead of searching cu_seqlens for its sentence.
+__global__ void __launch_bounds__(256)
+    token_positions(const int32_t *__restrict__ cu, int batch, int32_t *__restrict__ pos)
+{
+    const int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    grid_dep_wait();
+    grid_dep_launch();
+    if (s >= batch) return;
+    const int start = cu[s], len = cu[s + 1] - start;
+    for (int i = lane; i < len; i += 32) pos[start + i] = i;
+}
+
+// sin and cos of the rotary angle of (position, frequency index): inv_freq = theta^(-2 fi / HD),
+// angle = position * inv_freq in fp32.  Measured: the reduced hardware form is faster at
+// head_dim 128 (4 angles a lane), sincosf at 256 (8 angles a lane, 4 heads a token).
+template <int HD>
+__device__ __forceinline__ void rope_angle(int pos, int fi, float log2_theta, float &sn, float &cs)
+{
+    const float inv_freq = exp2f(-log2_theta * static_cast<float>(2 * fi) / static_cast<float>(HD));
+    if constexpr (HD == 128) sincos_reduced(static_cast<float>(pos) * inv_freq, sn, cs);
+    else sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+}
+
 template <int HD>
 __global__ void __launch_bounds__(256)
-    qk_norm_rope(__nv_bfloat16 *qkv, const int32_t *__restrict__ cu, int batch, int64_t total, int q_heads,
-                 int kv_heads, const float *__restrict__ q_w, const float *__restrict__ k_w, int one_plus, float eps,
-                 float log2_theta)
+    qk_norm_rope(__nv_bfloat16 *qkv, const int32_t *__restrict__ cu, const int32_t *__restrict__ tpos, int batch,
+                 int64_t total, int q_heads, int kv_heads, const float *__restrict__ q_w, const float *__restrict__ k_w,
+                 int one_plus, float eps, float log2_theta)
 {
     constexpr int E = HD / 32;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -209,17 +235,16 @@ __global__ void __launch_bounds__(256)
     grid_dep_wait();
     grid_dep_launch();
     if (t >= total) return;
-    const int pos = static_cast<int>(t - cu[sentence_of(cu, batch, t)]);
+    // the token's position in its sentence: from the positions array when given, else by
+    // binary search of cu_seqlens
+    const int pos = tpos ? tpos[t] : static_cast<int>(t - cu[sentence_of(cu, batch, t)]);
     float cs[E], sn[E], wq[E], wk[E];
+    const int f0 = (E * lane) & (HD / 2 - 1);  // this lane's first frequency index (E in a row)
+#pragma unroll
+    for (int i = 0; i < E; ++i) rope_angle<HD>(pos, f0 + i, log2_theta, sn[i], cs[i]);
 #pragma unroll
     for (int i = 0; i < E; ++i) {
         const int e = E * lane + i;
-        const int fi = e & (HD / 2 - 1);  // frequency index
-        const float inv_freq = exp2f(-log2_theta * static_cast<float>(2 * fi) / static_cast<float>(HD));
-        // measured: the reduced hardware form is faster at head_dim 128 (4 angles a lane),
-        // sincosf at 256 (8 angles a lane, 4 heads a token)
-        if constexpr (HD == 128) sincos_reduced(static_cast<float>(pos) * inv_freq, sn[i], cs[i]);
-        else sincosf(static_cast<float>(pos) * inv_freq, &sn[i], &cs[i]);
         wq[i] = q_w[e] + (one_plus ? 1.f : 0.f);
         wk[i] = k_w[e] + (one_plus ? 1.f : 0.f);
     }
@@ -339,20 +364,26 @@ cudaError_t launch_rms_sandwich(const void *y, const float *w_post, float *h32, 
 #undef FE_ROW_DISPATCH
 #undef FE_ROW_DISPATCH2
 
+cudaError_t launch_token_positions(const int32_t *cu, int batch, int32_t *pos, cudaStream_t s)
+{
+    if (batch == 0) return cudaSuccess;
+    return launch_k(token_positions, dim3(grid_rows(batch, 8)), dim3(256), 0, s, cu, batch, pos);
+}
+
 cudaError_t launch_qk_norm_rope(void *qkv, const int32_t *cu, int batch, int64_t total, int q_heads, int kv_heads,
                                 int head_dim, const float *q_w, const float *k_w, bool one_plus, float eps, float theta,
-                                cudaStream_t s)
+                                cudaStream_t s, const int32_t *pos)
 {
     if (total == 0) return cudaSuccess;
     const unsigned grid = grid_rows(total, 8);
     auto *p = static_cast<__nv_bfloat16 *>(qkv);
     const float lt = log2f(theta);
     if (head_dim == 128)
-        return launch_k(qk_norm_rope<128>, dim3(grid), dim3(256), 0, s, p, cu, batch, total, q_heads, kv_heads, q_w, k_w,
-                        one_plus ? 1 : 0, eps, lt);
+        return launch_k(qk_norm_rope<128>, dim3(grid), dim3(256), 0, s, p, cu, pos, batch, total, q_heads, kv_heads,
+                        q_w, k_w, one_plus ? 1 : 0, eps, lt);
     if (head_dim == 256)
-        return launch_k(qk_norm_rope<256>, dim3(grid), dim3(256), 0, s, p, cu, batch, total, q_heads, kv_heads, q_w, k_w,
-                        one_plus ? 1 : 0, eps, lt);
+        return launch_k(qk_norm_rope<256>, dim3(grid), dim3(256), 0, s, p, cu, pos, batch, total, q_heads, kv_heads,
+                        q_w, k_w, one_plus ? 1 : 0, eps, lt);
     return cudaErrorInvalidValue;
 }
 
