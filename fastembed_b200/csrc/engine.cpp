@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -636,6 +637,17 @@ struct DeviceGuard {
     ~DeviceGuard() { cudaSetDevice(prev); }
 };
 
+// Tokens per device pass of fe_engine_encode_host: FE_MAX_TOKENS_PER_PASS, else 262,144
+// (about 7 GB of bge-large activations).
+int64_t max_tokens_per_pass()
+{
+    if (const char *v = std::getenv("FE_MAX_TOKENS_PER_PASS")) {
+        const long long n = std::atoll(v);
+        if (n > 0) return n;
+    }
+    return 262144;
+}
+
 }  // namespace
 
 extern "C" {
@@ -852,32 +864,40 @@ fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t 
     if (batch == 0) return FE_OK;
     std::lock_guard<std::mutex> lk(e->mu);
     DeviceGuard g(e->device);
-    int64_t T = 0;
-    for (int b = 0; b < batch; ++b) {
+    for (int b = 0; b < batch; ++b)
         if (lengths[b] < 0 || lengths[b] > stride)
             return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_encode_host: length outside [0, stride]");
-        T += lengths[b];
-    }
     const size_t D = e->family == FE_FAMILY_BERT ? e->cfg.hidden : e->rc.hidden;
-    FE_TRY_CUDA(e->p_ids.ensure(std::max<int64_t>(T, 1) * 4));
-    FE_TRY_CUDA(e->p_cu.ensure((batch + 1) * 4));
-    FE_TRY_CUDA(e->p_out.ensure(batch * D * 4));
-    FE_TRY_CUDA(e->d_ids.ensure(std::max<int64_t>(T, 1) * 4));
-    FE_TRY_CUDA(e->d_cu.ensure((batch + 1) * 4));
-    FE_TRY_CUDA(e->d_out.ensure(batch * D * 4));
-    FE_TRY(fe_pack_batch(ids, lengths, batch, stride, e->p_ids.as<int32_t>(), e->p_cu.as<int32_t>()));
+    // Consecutive sentences run as one device pass of at most max_tokens_per_pass() tokens
+    // (a longer single sentence runs alone): activation memory stays bounded for any batch.
+    const int64_t cap = max_tokens_per_pass();
     cudaStream_t s = e->stream;
-    FE_TRY_CUDA(cudaMemcpyAsync(e->d_ids.p, e->p_ids.p, T * 4, cudaMemcpyHostToDevice, s));
-    FE_TRY_CUDA(cudaMemcpyAsync(e->d_cu.p, e->p_cu.p, (batch + 1) * 4, cudaMemcpyHostToDevice, s));
-    if (e->family != FE_FAMILY_BERT)
-        FE_TRY(forward_rms(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), batch,
+    for (int b0 = 0; b0 < batch;) {
+        int b1 = b0;
+        int64_t T = 0;
+        while (b1 < batch && (b1 == b0 || T + lengths[b1] <= cap)) T += lengths[b1++];
+        const int nb = b1 - b0;
+        FE_TRY_CUDA(e->p_ids.ensure(std::max<int64_t>(T, 1) * 4));
+        FE_TRY_CUDA(e->p_cu.ensure((nb + 1) * 4));
+        FE_TRY_CUDA(e->p_out.ensure(nb * D * 4));
+        FE_TRY_CUDA(e->d_ids.ensure(std::max<int64_t>(T, 1) * 4));
+        FE_TRY_CUDA(e->d_cu.ensure((nb + 1) * 4));
+        FE_TRY_CUDA(e->d_out.ensure(nb * D * 4));
+        FE_TRY(fe_pack_batch(ids + static_cast<size_t>(b0) * stride, lengths + b0, nb, stride, e->p_ids.as<int32_t>(),
+                             e->p_cu.as<int32_t>()));
+        FE_TRY_CUDA(cudaMemcpyAsync(e->d_ids.p, e->p_ids.p, T * 4, cudaMemcpyHostToDevice, s));
+        FE_TRY_CUDA(cudaMemcpyAsync(e->d_cu.p, e->p_cu.p, (nb + 1) * 4, cudaMemcpyHostToDevice, s));
+        if (e->family != FE_FAMILY_BERT)
+            FE_TRY(forward_rms(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), nb,
+                               e->d_out.as<float>(), s));
+        else
+            FE_TRY(forward(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), nb,
                            e->d_out.as<float>(), s));
-    else
-        FE_TRY(forward(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), batch,
-                       e->d_out.as<float>(), s));
-    FE_TRY_CUDA(cudaMemcpyAsync(e->p_out.p, e->d_out.p, batch * D * 4, cudaMemcpyDeviceToHost, s));
-    FE_TRY_CUDA(cudaStreamSynchronize(s));
-    std::memcpy(out, e->p_out.p, batch * D * 4);
+        FE_TRY_CUDA(cudaMemcpyAsync(e->p_out.p, e->d_out.p, nb * D * 4, cudaMemcpyDeviceToHost, s));
+        FE_TRY_CUDA(cudaStreamSynchronize(s));  // the pinned buffers are reused by the next pass
+        std::memcpy(out + static_cast<size_t>(b0) * D, e->p_out.p, nb * D * 4);
+        b0 = b1;
+    }
     int *w = fe::device_status_word(e->device);
     int v = 0;
     FE_TRY_CUDA(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));

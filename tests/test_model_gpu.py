@@ -137,3 +137,26 @@ def test_xlmr_positions_match_oracle(cuda_dev, oracle_lib):
     for b in (3, 7):  # batch invariance, bit for bit
         assert np.array_equal(eng.encode_host(ids[b:b + 1], lengths[b:b + 1])[0], got[b])
     eng.close()
+
+
+def test_host_encode_runs_large_batches_in_passes(cuda_dev, oracle_lib, monkeypatch):
+    """fe_engine_encode_host splits a batch into device passes of at most
+    FE_MAX_TOKENS_PER_PASS tokens (a longer sentence runs alone), so memory stays bounded
+    for any batch.  With a 100-token cap the 40 sentences run in many passes: rows match
+    the one-pass result within fp32 rounding (small passes take the 1-CTA GEMM and the
+    two-launch norm) and the oracle within the model tolerance."""
+    from fastembed_b200 import ops, workload as W
+    import dataclasses
+    shape = dataclasses.replace(W.SHAPES["bge-small"], layers=2)
+    weights = W.make_weights(shape, seed=21)
+    lengths = W.sample_lengths(shape, batch=40, seed=22)
+    lengths[5] = 128  # longer than the cap: a pass of its own
+    ids, _ = W.sample_ids(shape, lengths, seed=23, pad_to=128)
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(weights)
+    one_pass = eng.encode_host(ids, lengths)
+    monkeypatch.setenv("FE_MAX_TOKENS_PER_PASS", "100")
+    passes = eng.encode_host(ids, lengths)
+    eng.close()
+    assert np.abs(passes - one_pass).max() <= 1e-5
+    _check(passes, oracle_lib.Model(shape, weights).forward_batch(ids, lengths))
