@@ -860,7 +860,6 @@ fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t 
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_encode_host: bad arguments");
     if (fe_engine_missing_weights(e) != 0)
         return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_encode_host: weights not loaded");
-    if (batch > 65535) return fail(FE_ERR_UNSUPPORTED, "fe_engine_encode_host: batch too large");
     if (batch == 0) return FE_OK;
     std::lock_guard<std::mutex> lk(e->mu);
     DeviceGuard g(e->device);
@@ -869,13 +868,15 @@ fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t 
             return fail(FE_ERR_INVALID_ARGUMENT, "fe_engine_encode_host: length outside [0, stride]");
     const size_t D = e->family == FE_FAMILY_BERT ? e->cfg.hidden : e->rc.hidden;
     // Consecutive sentences run as one device pass of at most max_tokens_per_pass() tokens
-    // (a longer single sentence runs alone): activation memory stays bounded for any batch.
+    // (a longer single sentence runs alone) and kMaxPassSentences sentences (the device
+    // path's batch limit): activation memory stays bounded for any batch.
     const int64_t cap = max_tokens_per_pass();
+    constexpr int kMaxPassSentences = 65535;
     cudaStream_t s = e->stream;
     for (int b0 = 0; b0 < batch;) {
         int b1 = b0;
         int64_t T = 0;
-        while (b1 < batch && (b1 == b0 || T + lengths[b1] <= cap)) T += lengths[b1++];
+        while (b1 < batch && b1 - b0 < kMaxPassSentences && (b1 == b0 || T + lengths[b1] <= cap)) T += lengths[b1++];
         const int nb = b1 - b0;
         FE_TRY_CUDA(e->p_ids.ensure(std::max<int64_t>(T, 1) * 4));
         FE_TRY_CUDA(e->p_cu.ensure((nb + 1) * 4));

@@ -329,8 +329,8 @@ fe_status fe_engine_encode_packed(fe_engine *e, const int32_t *ids, const int32_
  * padded), lengths host int32 [batch]; out is host fp32 [batch, hidden].  Copies
  * in, runs, copies out and synchronises.  Consecutive sentences run as one device
  * pass of at most FE_MAX_TOKENS_PER_PASS tokens (default 262,144; a longer sentence
- * runs alone), so device memory stays bounded for any batch, as the reference's
- * one-sentence-at-a-time loop does.  The token-id form of
+ * runs alone) and 65,535 sentences, so device memory stays bounded for any batch, as
+ * the reference's one-sentence-at-a-time loop does.  The token-id form of
  * SentenceTransformerImpl::encode_batch (src/sentence_transformers_impl.cpp:359-365). */
 fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t *lengths,
                                 int32_t batch, int32_t stride, float *out);

@@ -160,3 +160,24 @@ def test_host_encode_runs_large_batches_in_passes(cuda_dev, oracle_lib, monkeypa
     eng.close()
     assert np.abs(passes - one_pass).max() <= 1e-5
     _check(passes, oracle_lib.Model(shape, weights).forward_batch(ids, lengths))
+
+
+def test_host_encode_more_sentences_than_one_pass_takes(cuda_dev):
+    """70,000 two-token sentences: more than a device pass takes (65,535), so the call
+    runs two passes.  The rows around the boundary equal a separate small call within
+    fp32 rounding."""
+    from fastembed_b200 import ops, workload as W
+    import dataclasses
+    shape = dataclasses.replace(W.SHAPES["bge-small"], layers=1)
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(W.make_weights(shape, seed=31))
+    rng = np.random.default_rng(32)
+    n = 70000
+    ids = np.stack([np.full(n, 101), rng.integers(1000, shape.vocab, n)], 1).astype(np.int32)
+    lengths = np.full(n, 2, np.int32)
+    out = eng.encode_host(ids, lengths)
+    assert out.shape == (n, shape.hidden) and np.isfinite(out).all()
+    lo, hi = 65530, 65541
+    part = eng.encode_host(ids[lo:hi], lengths[lo:hi])
+    eng.close()
+    assert np.abs(out[lo:hi] - part).max() <= 1e-5
