@@ -181,3 +181,29 @@ def test_host_encode_more_sentences_than_one_pass_takes(cuda_dev):
     part = eng.encode_host(ids[lo:hi], lengths[lo:hi])
     eng.close()
     assert np.abs(out[lo:hi] - part).max() <= 1e-5
+
+
+@pytest.mark.parametrize("family", ["bert", "qwen3", "gemma3"])
+def test_empty_sentence_in_batch(cuda_dev, family):
+    """A zero-length sentence inside a batch gives a zero row and leaves every other row
+    as the batch without it gives it (bit for bit: the same passes run on the same tokens)."""
+    from fastembed_b200 import ops, workload as W
+    import dataclasses
+    if family == "bert":
+        shape = dataclasses.replace(W.SHAPES["bge-small"], layers=2)
+        weights = W.make_weights(shape, seed=41)
+        lengths = np.array([5, 0, 17, 0, 9], np.int32)
+        ids, _ = W.sample_ids(shape, np.maximum(lengths, 2), seed=42, pad_to=32)  # rows of length 0 unused
+    else:
+        shape = W.RMS_SHAPES["qwen3-tiny" if family == "qwen3" else "gemma3-tiny"]
+        weights = W.make_rms_weights(shape, seed=41)
+        lengths = np.array([5, 0, 17, 0, 9], np.int32)
+        ids = W.sample_rms_ids(shape, np.maximum(lengths, 2), seed=42)
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(weights)
+    got = eng.encode_host(ids, lengths)
+    keep = lengths > 0
+    ref = eng.encode_host(ids[keep], lengths[keep])
+    eng.close()
+    assert np.all(got[~keep] == 0)
+    assert np.array_equal(got[keep], ref)
