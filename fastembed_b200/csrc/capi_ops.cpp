@@ -38,7 +38,7 @@ fe_status fe_sgemm_nn(const float *a, const float *b, float *c, int64_t m, int64
                       fe_stream_t stream)
 {
     if (m < 0 || n < 0 || k < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nn: negative size");
-    if ((m * k) && (!c || (n && (!a || !b)))) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nn: null pointer");
+    if (m && k && (!c || (n && (!a || !b)))) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nn: null pointer");
     return done(fe::launch_sgemm(a, b, nullptr, c, m, n, k, false, cs(stream)), "fe_sgemm_nn");
 }
 
@@ -46,7 +46,7 @@ fe_status fe_sgemm_nt(const float *a, const float *b, const float *bias, float *
                       int64_t k, fe_stream_t stream)
 {
     if (m < 0 || n < 0 || k < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nt: negative size");
-    if ((m * k) && (!c || (n && (!a || !b)))) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nt: null pointer");
+    if (m && k && (!c || (n && (!a || !b)))) return fail(FE_ERR_INVALID_ARGUMENT, "fe_sgemm_nt: null pointer");
     return done(fe::launch_sgemm(a, b, bias, c, m, n, k, true, cs(stream)), "fe_sgemm_nt");
 }
 

@@ -7,7 +7,7 @@
  * (include/ops/cuda/cuda_attention_ops.cuh:6-22) and SentenceTransformer
  * (include/sentence_transformers.h:12-40).  Each entry point below names the
  * reference routine it replaces.  The C++ classes of the same names in this
- * repository (include/ops/cuda/*, include/sentence_transformers.h) are thin
+ * repository (the headers under include/ops/cuda and include/sentence_transformers.h) are thin
  * wrappers over these functions.
  *
  * Conventions
