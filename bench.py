@@ -9,12 +9,14 @@ length and cut into N contiguous slices of equal algorithmic FLOPs: replica data
 parallelism with no collective on the data path (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload bge-large|bge-small|bge-base|qwen3-0.6b|gemma-300m]
 
 Prints one JSON line on rank 0.  `value` is device-timed with inputs resident in
 HBM; `e2e` goes through the C ABI's host-buffer entry point (H2D of the ids and
 D2H of the embeddings inside the timed region).  `--impl reference` times the
-reference's own CPU ops (oracle/_ref, compiled from the reference sources) on a
-bounded sample of the same workload with all host cores.
+reference's own CPU ops (oracle/_ref, compiled from the reference sources) with all
+host threads on a stratified sample of the same workload: every 16th sentence of the
+length-sorted batch, the longest included, each timed on its own thread.
 """
 from __future__ import annotations
 
@@ -37,17 +39,26 @@ from fastembed_b200 import workload as W  # noqa: E402
 METRIC = "sentences/s bge-large b=256 L=512 @1/2/4/8 B200; attn+GEMM % TC peak"
 UNIT = "sentences/s"
 WORKLOAD = "bge-large"
-# --workload: the headline bge-large shape (default) or the Qwen3 / Gemma3 shapes, which
-# the reference has no path for (no CPU baseline; informational lines)
+# --workload: the headline bge-large shape (default), the bge-small / bge-base shapes, or
+# the Qwen3 / Gemma3 shapes, which the reference has no path for (no CPU baseline)
 DESCRIPTIONS = {
+    "bge-small": "bge-small shape (4L, D512, 8x64 heads, F2048 GELU, post-LN, CLS+L2), 8 sentences per GPU, "
+                 "lengths U[16,128], packed without padding, seeded N(0,0.02) weights",
+    "bge-base": "bge-base shape (12L, D768, 12x64 heads, F3072 GELU, post-LN, CLS+L2), 64 sentences per GPU, "
+                "lengths U[32,512], packed without padding, seeded N(0,0.02) weights",
     "bge-large": "bge-large shape (24L, D1024, 16x64 heads, F4096 GELU, post-LN, CLS+L2), 256 sentences per GPU, "
                  "lognormal lengths median 96 sigma 0.6 in [8,512], packed without padding, seeded N(0,0.02) weights",
-    "qwen3-0.6b": "Qwen3-0.6B shape (28L, D1024, 16q/8kv x 128 heads, causal, RoPE 1e6, F3072 SwiGLU, pre-RMSNorm, "
-                  "last-token+L2), 128 sentences per GPU, lengths U[64,1024], packed, seeded N(0,0.02) weights",
+    "qwen3-0.6b": "Qwen3-0.6B shape (28L, D1024, 16q/8kv x 128 heads, vocab 151669, causal, RoPE 1e6, F3072 SwiGLU, "
+                  "pre-RMSNorm, last-token+L2), 128 sentences per GPU, lengths U[64,1024], packed, seeded N(0,0.02) "
+                  "weights rounded to bf16",
     "gemma-300m": "Gemma-300M shape (24L, D768, 3q/1kv x 256 heads, bidirectional, RoPE 1e4/1e6, F1152 GeGLU, "
                   "sandwich RMSNorm, mean+L2), 512 sentences per GPU, lengths U[8,256], packed, seeded N(0,0.02) "
                   "weights",
 }
+
+
+def metric_name(workload):
+    return METRIC if workload == WORKLOAD else f"sentences/s {workload} @1/2/4/8 B200"
 
 
 def workload_shape(name):
@@ -139,69 +150,105 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU side
-def cpu_sample(shape, lengths_sorted, ids_sorted, cores, budget_s, per_core_gflops=1.5):
-    """A bounded, length-stratified sample: up to `cores` sentences (one per thread)
-    whose single-sentence cost fits the time budget at the reference's ~1.5 GFLOP/s/core."""
-    cap = per_core_gflops * 1e9 * budget_s
-    ok = np.array([shape.flops_per_sentence(int(L)) <= cap for L in lengths_sorted])
-    pool = np.nonzero(ok)[0]
-    if pool.size == 0:
-        pool = np.array([lengths_sorted.size - 1])
-    n = min(cores, pool.size)
-    pick = pool[np.unique(np.linspace(0, pool.size - 1, n).round().astype(int))]
-    return pick
+def cpu_plan(shape, lengths_sorted, cores):
+    """The stratified sample the CPU legs time: every `stride`-th sentence of the
+    length-sorted batch, longest first (so the longest sentence is always in it), with
+    at least one sentence per host thread (16 at the least, 64 at most).  `depth` is
+    how many encoder layers each sampled sentence runs: all of them when the longest
+    sampled sentence takes under ~8 s at the reference's ~2 GFLOP/s per core, else one
+    (every layer has the same shapes, so the per-layer time scales by the depth)."""
+    n = lengths_sorted.size
+    want = min(64, max(16, cores))
+    stride = max(1, n // want)
+    pick = np.arange(0, n, stride)
+    longest = shape.flops_per_sentence(int(lengths_sorted[pick].max())) if pick.size else 0.0
+    depth = shape.layers if longest <= 8 * 2e9 else 1
+    return pick, stride, depth
 
 
-def run_cpu_reference(shape, lengths_sorted, ids_sorted, weights, steps, warmup, budget_total_s):
-    """Times the reference's own CPU forward (oracle/_ref) on bounded samples; returns
-    (sentences/s extrapolated to the full batch's length mix, details)."""
+def _time_sentences(model, ids, lens, kind, threads):
+    """Per-sentence wall times of the reference's single-sentence forward, `threads`
+    sentences in flight at once (one per host thread, longest first)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    def one(i):
+        t0 = time.perf_counter()
+        model.forward(ids[i, :int(lens[i])], kind=kind)  # ctypes releases the GIL
+        return time.perf_counter() - t0
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        return np.array(list(ex.map(one, range(lens.size))), dtype=np.float64)
+
+
+def run_cpu_reference(shape, lengths_sorted, ids_sorted, weights, steps, warmup, single_thread=False):
+    """Times the reference's own CPU forward (oracle/_ref: its src/ops/cpu ops driven by
+    the restated bge_forward) on the stratified sample of cpu_plan, all host threads busy.
+
+    Each sampled sentence stands for `stride` sentences of the batch, and a sample run
+    at depth d < layers stands for layers / d times its time.  The whole batch's CPU
+    time is therefore estimated as stride * (layers / d) * sum(per-sentence times), and
+    sentences/s on T threads as batch * T / that (sentences are independent, so T
+    threads share a batch of hundreds of sentences evenly).  With `single_thread` the
+    sample also runs once on one thread, for the reference's own serial encode_batch
+    (src/sentence_transformers_impl.cpp:359-365)."""
+    import dataclasses
     from oracle import oracle as O
     kind = "ref" if O.available("ref") else "port"
-    model = O.Model(shape, weights)
     cores = os.cpu_count() or 1
-    per_step = max(2.0, budget_total_s / max(1, steps + warmup))
-    pick = cpu_sample(shape, lengths_sorted, ids_sorted, cores, per_step)
-    flops_pick = sum(shape.flops_per_sentence(int(L)) for L in lengths_sorted[pick])
+    pick, stride, depth = cpu_plan(shape, lengths_sorted, cores)
+    model = O.Model(dataclasses.replace(shape, layers=depth), weights)
     ids = np.ascontiguousarray(ids_sorted[pick])
     lens = np.ascontiguousarray(lengths_sorted[pick])
+    threads = int(min(cores, lens.size))
+    scale = stride * shape.layers / depth
     for _ in range(warmup):
-        model.forward_batch(ids, lens, kind=kind, threads=cores)
+        _time_sentences(model, ids, lens, kind, threads)
     t0 = time.perf_counter()
-    for _ in range(steps):
-        model.forward_batch(ids, lens, kind=kind, threads=cores)
-    dt = (time.perf_counter() - t0) / max(1, steps)
-    rate_flops = flops_pick / dt
-    total_flops = sum(shape.flops_per_sentence(int(L)) for L in lengths_sorted)
-    sent_s = lengths_sorted.size / (total_flops / rate_flops)
-    return sent_s, {
+    per_step = []
+    for _ in range(max(1, steps)):
+        per_step.append(_time_sentences(model, ids, lens, kind, threads).sum() * scale)
+    wall = (time.perf_counter() - t0) / max(1, steps)
+    batch = lengths_sorted.size
+    cpu_s = float(np.mean(per_step))  # estimated CPU seconds of the whole batch
+    sent_s = batch * threads / cpu_s
+    depth_txt = f"all {depth}" if depth == shape.layers else f"{depth} of {shape.layers}"
+    info = {
         "kind": "reference" if kind == "ref" else "port",
-        "cores": int(min(cores, len(pick))),
-        "sample": (f"{len(pick)} sentences (lengths {int(lens.min())}-{int(lens.max())}, length-stratified, one "
-                   f"per thread) per step, {dt:.2f} s/step, {rate_flops / 1e9:.1f} GFLOP/s; sentences/s "
-                   f"extrapolated by FLOPs to the full {lengths_sorted.size}-sentence length mix"),
-        "sample_sentences_per_s": len(pick) / dt,
-        "gflops": rate_flops / 1e9,
+        "cores": threads,
+        "sample": (f"{lens.size} sentences, every {stride}th of the {batch}-sentence batch sorted by length "
+                   f"(lengths {int(lens.min())}-{int(lens.max())}, the longest included), {depth_txt} layers "
+                   f"each, one sentence per thread on {threads} threads, {wall:.1f} s per step; sentences/s = "
+                   f"{batch} x {threads} threads / ({stride} x {shape.layers // depth} x the summed "
+                   f"per-sentence times)"),
+        "batch_cpu_seconds": cpu_s,
+        "tokens_per_s": float(lengths_sorted.sum()) * threads / cpu_s,
     }
+    if single_thread:
+        t1 = _time_sentences(model, ids, lens, kind, 1).sum() * scale
+        info["single_thread"] = {"value": batch / t1, "unit": UNIT, "cores": 1,
+                                 "tokens_per_s": float(lengths_sorted.sum()) / t1,
+                                 "sample": "the same sample run once on one thread"}
+    return sent_s, info
 
 
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    shape = W.SHAPES[WORKLOAD]
-    lengths, ids = global_batch(shape, 1)
+    shape = W.SHAPES[args.workload]
+    lengths, ids = global_batch(shape, 1, args.batch)
     weights = W.make_weights(shape)
     steps, warmup = args.steps, args.warmup
-    value, info = run_cpu_reference(shape, lengths, ids, weights, steps, warmup, budget_total_s=150.0)
+    value, info = run_cpu_reference(shape, lengths, ids, weights, steps, warmup, single_thread=True)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": steps, "warmup": warmup, "higher_is_better": True, "scaling": "weak",
+        "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": steps, "warmup": warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "bge-large shape (24L, D1024, 16x64 heads, F4096), batch 256, lognormal lengths "
-                               "median 96 sigma 0.6 in [8,512], seeded N(0,0.02) weights",
-                   "global_batch": shape.batch, "parallelism": "host threads"},
+        "config": {"workload": DESCRIPTIONS[args.workload], "global_batch": int(lengths.size),
+                   "valid_tokens_per_step": int(lengths.sum()), "tokens_per_s": info["tokens_per_s"],
+                   "parallelism": f"{info['cores']} host threads, one sentence per thread"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": info["cores"], "kind": info["kind"],
-                         "sample": info["sample"]},
+                         "sample": info["sample"], "single_thread": info["single_thread"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -329,19 +376,19 @@ def ours(args):
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not rms:
-        v, info = run_cpu_reference(shape, lengths_all, ids_all, weights, steps=1, warmup=0, budget_total_s=20.0)
+        v, info = run_cpu_reference(shape, lengths_all, ids_all, weights, steps=1, warmup=0)
         cpu_base = {"value": v, "unit": UNIT, "cores": info["cores"], "kind": info["kind"], "sample": info["sample"]}
 
     if rank == 0:
         traffic = None
         tpath = os.path.join(ROOT, "profiles", "linear_tcgen05_pair_bge-large.md")
-        if os.path.exists(tpath) and not rms:
+        if os.path.exists(tpath) and args.workload == "bge-large":
             with open(tpath) as f:
                 for ln in f:
                     if ln.startswith("traffic_bytes_per_launch:"):
                         traffic = int(ln.split(":")[1])
         line = {
-            "metric": METRIC if args.workload == WORKLOAD else f"sentences/s {args.workload} @1/2/4/8 B200",
+            "metric": metric_name(args.workload),
             "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -389,12 +436,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="sentences per GPU (default: the workload's)")
     ap.add_argument("--workload", choices=sorted(DESCRIPTIONS), default=WORKLOAD,
-                    help="bge-large (the headline) or the Qwen3 / Gemma3 shapes (informational)")
+                    help="bge-large (the headline), bge-small / bge-base, or the Qwen3 / Gemma3 shapes")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
-        if args.workload != WORKLOAD:
+        if args.workload not in W.SHAPES:
             if int(os.environ.get("RANK", "0")) == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "the reference has no Qwen3 / Gemma3 forward"}))
             return 0

@@ -222,6 +222,7 @@ class RmsShape:
     full_every: int = 0
     batch: int = 8
     lengths: tuple = ("uniform", 16, 128)
+    bf16_weights: bool = False  # weights drawn in FP32, then rounded to the nearest bf16 value
 
     @property
     def pooling(self) -> str:
@@ -248,9 +249,9 @@ class RmsShape:
 
 RMS_SHAPES = {
     # Qwen3-0.6B shape: 28 layers, D 1024, 16 q / 8 kv heads x 128, FFN 3072 SwiGLU, causal;
-    # batch 128, L ~ U[64, 1024]
-    "qwen3-0.6b": RmsShape("qwen3-0.6b", "qwen3", 28, 1024, 16, 8, 128, 3072, 151936, batch=128,
-                           lengths=("uniform", 64, 1024)),
+    # batch 128, L ~ U[64, 1024]; vocab 151,669; BF16 weights
+    "qwen3-0.6b": RmsShape("qwen3-0.6b", "qwen3", 28, 1024, 16, 8, 128, 3072, 151669, batch=128,
+                           lengths=("uniform", 64, 1024), bf16_weights=True),
     # Gemma-300M (EmbeddingGemma) shape: 24 layers, D 768, 3 q / 1 kv heads x 256, FFN 1152
     # GeGLU, bidirectional, every 6th layer global; batch 512, L ~ U[8, 256]
     "gemma-300m": RmsShape("gemma-300m", "gemma3", 24, 768, 3, 1, 256, 1152, 262144, max_pos=2048,
@@ -292,10 +293,18 @@ def rms_weight_names(shape: RmsShape) -> list[tuple[str, tuple[int, ...], str]]:
     return out
 
 
+def round_to_bf16(a: np.ndarray) -> np.ndarray:
+    """FP32 values rounded to the nearest bf16 value (ties to even), kept as FP32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
 def make_rms_weights(shape: RmsShape, seed: int = 0, std: float = 0.02,
                      norm_jitter: float = 0.0) -> dict[str, np.ndarray]:
-    """Seeded random-init FP32 weights keyed by HF name; `norm_jitter` adds N(0, jitter)
-    to the norm weights (tests use it so that the weight form matters)."""
+    """Seeded random-init weights keyed by HF name (FP32 arrays; bf16 values when the
+    shape has `bf16_weights`); `norm_jitter` adds N(0, jitter) to the norm weights
+    (tests use it so that the weight form matters)."""
     rng = np.random.default_rng(seed)
     w: dict[str, np.ndarray] = {}
     for name, shp, init in rms_weight_names(shape):
@@ -305,7 +314,7 @@ def make_rms_weights(shape: RmsShape, seed: int = 0, std: float = 0.02,
             a = np.ones(shp, dtype=np.float32) if init == "ones" else np.zeros(shp, dtype=np.float32)
             if norm_jitter:
                 a = a + rng.standard_normal(size=shp, dtype=np.float32) * np.float32(norm_jitter)
-        w[name] = a
+        w[name] = round_to_bf16(a) if shape.bf16_weights else a
     return w
 
 

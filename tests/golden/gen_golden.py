@@ -82,17 +82,31 @@ def gen_ops() -> None:
         json.dump(meta, f, indent=1, sort_keys=True)
 
 
-def pick(lengths: np.ndarray, quantiles) -> list[int]:
-    order = np.argsort(lengths, kind="stable")
-    return sorted({int(order[min(len(order) - 1, int(round(q * (len(order) - 1))))]) for q in quantiles})
+def stride_pick(lengths: np.ndarray, stride: int) -> list[int]:
+    """Every `stride`-th sentence of the batch sorted by length, longest first: a
+    length-stratified sample that always holds the longest sentence."""
+    order = np.argsort(-lengths, kind="stable")
+    return sorted(int(i) for i in order[::stride])
 
 
-def gen_model(name: str, quantiles=None) -> None:
+# maximum and edge lengths at the bge-large depth: the position-table limit 512, query-tile
+# boundaries 128 / 129 / 257, and one- and two-token sentences
+EDGE_LENGTHS = (512, 511, 257, 129, 128, 2, 1)
+EDGE_SEED = 3
+
+
+def edge_inputs(shape):
+    lengths = np.array(EDGE_LENGTHS, np.int32)
+    ids, _ = W.sample_ids(shape, lengths, seed=EDGE_SEED, pad_to=512)
+    return lengths, ids
+
+
+def gen_model(name: str, stride: int = 1) -> None:
     shape = W.SHAPES[name]
     weights = W.make_weights(shape)
     lengths = W.sample_lengths(shape)
     ids, _ = W.sample_ids(shape, lengths)
-    idx = list(range(shape.batch)) if quantiles is None else pick(lengths, quantiles)
+    idx = stride_pick(lengths, stride)
     t0 = time.time()
     emb = O.Model(shape, weights).forward_batch(ids[idx], lengths[idx], kind="ref",
                                                 threads=os.cpu_count())
@@ -102,15 +116,28 @@ def gen_model(name: str, quantiles=None) -> None:
                         weights_sha256=np.array(weights_hash(weights)))
 
 
+def gen_edge(name: str) -> None:
+    shape = W.SHAPES[name]
+    weights = W.make_weights(shape)
+    lengths, ids = edge_inputs(shape)
+    t0 = time.time()
+    emb = O.Model(shape, weights).forward_batch(ids, lengths, kind="ref", threads=os.cpu_count())
+    print(f"{name} edge lengths {lengths.tolist()} in {time.time() - t0:.1f}s")
+    np.savez_compressed(os.path.join(HERE, f"model_{name}-edge.npz"), lengths=lengths, embeddings=emb,
+                        ids_sha256=np.array(sha(ids)), weights_sha256=np.array(weights_hash(weights)))
+
+
 if __name__ == "__main__":
     if not O.available("ref"):
         sys.exit("oracle/_ref is not built (make -C oracle with the reference sources present)")
-    what = sys.argv[1:] or ["ops", "bge-small", "bge-base", "bge-large"]
+    what = sys.argv[1:] or ["ops", "bge-small", "bge-base", "bge-large", "bge-large-edge"]
     if "ops" in what:
         gen_ops()
     if "bge-small" in what:
-        gen_model("bge-small")
+        gen_model("bge-small")  # the whole batch of 8
     if "bge-base" in what:
-        gen_model("bge-base", quantiles=(0.0, 0.5, 1.0))
+        gen_model("bge-base")  # the whole batch of 64
     if "bge-large" in what:
-        gen_model("bge-large", quantiles=(0.0, 0.5, 0.9, 1.0))
+        gen_model("bge-large", stride=8)  # 32 of 256, every 8th by length, the longest included
+    if "bge-large-edge" in what:
+        gen_edge("bge-large")

@@ -12,10 +12,12 @@ COS_MIN = 0.9999
 MAXABS = 2e-3
 
 
-def _check(got, ref):
+def _check(got, ref, label=""):
     cos = (got * ref).sum(1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(ref, axis=1))
+    err = np.abs(got - ref).max(axis=1)
+    print(f"{label}: {got.shape[0]} sentences, min cos {cos.min():.7f}, max abs {err.max():.3e}")
     assert cos.min() >= COS_MIN, cos.min()
-    assert np.abs(got - ref).max() <= MAXABS, np.abs(got - ref).max()
+    assert err.max() <= MAXABS, err.max()
 
 
 def test_bge_small_batch_matches_oracle(cuda_dev, oracle_lib):
@@ -73,9 +75,11 @@ def test_rejects_too_long_and_bad_ids(cuda_dev):
 
 @pytest.mark.parametrize("name", ["bge-small", "bge-base", "bge-large"])
 def test_engine_matches_reference_golden(cuda_dev, name):
-    """Stored embeddings of the reference's own CPU forward (tests/golden/model_*.npz,
-    length-stratified sentences for the base and large shapes) on the same seeded
-    weights and ids; the sentences run inside their full batch on the GPU."""
+    """Stored embeddings of the reference's own CPU forward (tests/golden/model_*.npz:
+    every sentence of the bge-small and bge-base batches, and every 8th sentence of the
+    length-sorted bge-large batch, 32 of 256, the longest included) on the same seeded
+    weights and ids; the sentences run inside their full batch on the GPU, and every
+    stored sentence must meet the tolerance."""
     import os
     from fastembed_b200 import ops, workload as W
     from tests.golden import gen_golden as G
@@ -89,7 +93,28 @@ def test_engine_matches_reference_golden(cuda_dev, name):
     eng = ops.Engine(shape, 0)
     eng.load_weights(weights)
     got = eng.encode_host(ids, lengths)
-    _check(got[gold["index"]], gold["embeddings"])
+    assert np.array_equal(lengths[gold["index"]], gold["lengths"])
+    _check(got[gold["index"]], gold["embeddings"], name)
+    eng.close()
+
+
+def test_engine_matches_reference_golden_edge_lengths(cuda_dev):
+    """The full 24-layer bge-large shape at the position-table maximum (512 tokens), the
+    query-tile boundaries 128 / 129 / 257 and one- and two-token sentences, against the
+    reference's own CPU forward (tests/golden/model_bge-large-edge.npz)."""
+    import os
+    from fastembed_b200 import ops, workload as W
+    from tests.golden import gen_golden as G
+    gold = np.load(os.path.join(os.path.dirname(__file__), "golden", "model_bge-large-edge.npz"))
+    shape = W.SHAPES["bge-large"]
+    weights = W.make_weights(shape)
+    assert G.weights_hash(weights) == str(gold["weights_sha256"]), "weight generator changed"
+    lengths, ids = G.edge_inputs(shape)
+    assert G.sha(ids) == str(gold["ids_sha256"]), "id generator changed"
+    assert np.array_equal(lengths, gold["lengths"])
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(weights)
+    _check(eng.encode_host(ids, lengths), gold["embeddings"], "bge-large edge")
     eng.close()
 
 

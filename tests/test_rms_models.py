@@ -13,6 +13,7 @@ import pytest
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 SHAPES = ("qwen3-tiny", "gemma3-tiny")
+FULL = ("qwen3-0.6b", "gemma-300m")  # the benchmark shapes at full depth
 
 
 def _golden(name):
@@ -79,4 +80,45 @@ def test_engine_matches_hf_edge_lengths(cuda_dev, name):
     eng.close()
     cmin, err = _close(got, ref)
     assert cmin >= 0.9999 and err <= 2e-3, (cmin, err)
+    ops.device_status(0)
+
+
+@pytest.mark.parametrize("name", FULL)
+def test_full_golden_inputs_regenerate(name):
+    """The full-shape goldens were made from the benchmark's weights and batch."""
+    from tests.golden import gen_golden_rms as G
+    g = _golden(name)
+    shape, weights, lengths, ids, index = G.full_inputs(name)
+    assert np.array_equal(g["index"], index) and np.array_equal(g["lengths"], lengths[index])
+    assert str(g["digest"]) == G.digest(weights, ids)
+    e = _golden(f"{name}-edge")
+    el, eids = G.edge_inputs(shape)
+    assert np.array_equal(e["lengths"], el) and str(e["digest"]) == G.digest(weights, eids)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", FULL)
+def test_engine_matches_full_depth_golden(cuda_dev, name):
+    """The Qwen3-0.6B shape (28 layers x 1024, causal GQA, bf16-valued weights, 128
+    sentences of U[64, 1024] tokens) and the EmbeddingGemma-300M shape (24 layers x 768,
+    512 sentences of U[8, 256]) at full depth: the stored sentences (every 16th / 32nd
+    of the batch by length, the longest included) run inside the whole benchmark batch,
+    then an edge set up to 1024 tokens; each against transformers in FP32."""
+    from fastembed_b200 import ops
+    from tests.golden import gen_golden_rms as G
+    g = _golden(name)
+    shape, weights, lengths, ids, index = G.full_inputs(name)
+    eng = ops.Engine(shape, 0)
+    eng.load_weights(weights)
+    got = eng.encode_host(ids, lengths)[index]
+    cmin, err = _close(got, g["embeddings"])
+    print(f"{name}: {index.size} sentences of the batch, min cos {cmin:.7f}, max abs {err:.3e}")
+    assert cmin >= 0.9999 and err <= 2e-3, (cmin, err)
+    e = _golden(f"{name}-edge")
+    el, eids = G.edge_inputs(shape)
+    got = eng.encode_host(eids, el)
+    cmin, err = _close(got, e["embeddings"])
+    print(f"{name}: edge lengths {el.tolist()}, min cos {cmin:.7f}, max abs {err:.3e}")
+    assert cmin >= 0.9999 and err <= 2e-3, (cmin, err)
+    eng.close()
     ops.device_status(0)
