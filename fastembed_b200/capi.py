@@ -61,6 +61,7 @@ _SIGS = {
     "fe_status_string": ([C.c_int], C.c_char_p),
     "fe_last_error_message": ([], C.c_char_p),
     "fe_device_status": ([C.c_int], C.c_int),
+    "fe_set_wait_limit": ([C.c_int, C.c_uint64], C.c_int),
     "fe_version": ([], C.c_char_p),
     "fe_sgemm_nn": ([vp, vp, vp, i64, i64, i64, vp], C.c_int),
     "fe_sgemm_nt": ([vp, vp, vp, vp, i64, i64, i64, vp], C.c_int),

@@ -121,7 +121,7 @@ struct fe_engine {
     int64_t cap_tokens = 0;
     // per-call inputs for the host path
     DevBuf d_ids, d_cu, d_out;
-    PinnedBuf p_ids, p_cu, p_out;
+    PinnedBuf p_ids, p_cu, p_out, p_status;
 
     // profiling
     bool profiling = false;
@@ -873,6 +873,9 @@ fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t 
     const int64_t cap = max_tokens_per_pass();
     constexpr int kMaxPassSentences = 65535;
     cudaStream_t s = e->stream;
+    int *w = fe::device_status_word(e->device);
+    if (!w) return fail(FE_ERR_CUDA, "fe_engine_encode_host: no device status word");
+    FE_TRY_CUDA(e->p_status.ensure(sizeof(int)));
     for (int b0 = 0; b0 < batch;) {
         int b1 = b0;
         int64_t T = 0;
@@ -895,17 +898,19 @@ fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t 
             FE_TRY(forward(e, e->d_ids.as<int32_t>(), e->d_cu.as<int32_t>(), e->p_cu.as<int32_t>(), nb,
                            e->d_out.as<float>(), s));
         FE_TRY_CUDA(cudaMemcpyAsync(e->p_out.p, e->d_out.p, nb * D * 4, cudaMemcpyDeviceToHost, s));
+        // the device status word comes back with the embeddings: a pass whose kernels met a
+        // bad token id or a wait that ran out ends the call before the next pass starts
+        FE_TRY_CUDA(cudaMemcpyAsync(e->p_status.p, w, sizeof(int), cudaMemcpyDeviceToHost, s));
         FE_TRY_CUDA(cudaStreamSynchronize(s));  // the pinned buffers are reused by the next pass
+        const int v = *e->p_status.as<int>();
+        if (v != 0) {
+            FE_TRY_CUDA(cudaMemsetAsync(w, 0, sizeof(int), s));
+            FE_TRY_CUDA(cudaStreamSynchronize(s));
+            if (v == fe::DEV_BAD_INPUT) return fail(FE_ERR_INVALID_ARGUMENT, "token id outside the vocabulary");
+            return fail(FE_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait ran out");
+        }
         std::memcpy(out + static_cast<size_t>(b0) * D, e->p_out.p, nb * D * 4);
         b0 = b1;
-    }
-    int *w = fe::device_status_word(e->device);
-    int v = 0;
-    FE_TRY_CUDA(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
-    if (v != 0) {
-        cudaMemset(w, 0, sizeof(int));
-        if (v == fe::DEV_BAD_INPUT) return fail(FE_ERR_INVALID_ARGUMENT, "token id outside the vocabulary");
-        return fail(FE_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait ran out");
     }
     return FE_OK;
 }

@@ -15,6 +15,20 @@ namespace fe {
 // A bounded wait gives up after this many nanoseconds of %globaltimer; any wait
 // that is correct finishes in microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Limits below this are checked at every poll instead of every 256th.
+constexpr uint64_t kShortWaitNs = 1000000ull;
+
+// The limit of the waits that guard work (a stage, an accumulator, a peer's row
+// statistics), settable per device and per kernel file through fe_set_wait_limit: each
+// .cu file that includes this header has its own copy, set by its own
+// set_wait_limit_*() host function.  The drain waits that let a CTA's own copies and
+// MMAs land before it exits (mbar_wait_drain) always use kWaitLimitNs.
+static __constant__ uint64_t c_wait_limit_ns = kWaitLimitNs;
+
+static inline cudaError_t set_wait_limit_this_file(uint64_t ns)
+{
+    return cudaMemcpyToSymbol(c_wait_limit_ns, &ns, sizeof(ns));
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
 {
@@ -110,9 +124,26 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t wait_limit_ns() { return c_wait_limit_ns; }
+
 // Waits for the phase with the given parity to complete.  Returns false (and the
-// caller must abandon its work) if kWaitLimitNs elapses first.
+// caller must abandon its work) if the work-wait limit (wait_limit_ns) elapses first.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t limit = wait_limit_ns();
+    const bool every = limit < kShortWaitNs;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (((i & 255u) == 0 || every) && globaltimer_ns() - t0 > limit) return false;
+    }
+}
+
+// mbar_wait for the drain before a CTA exits: waits for copies and MMAs that this CTA
+// started, which always complete, so it keeps the fixed kWaitLimitNs whatever the
+// work-wait limit is.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();

@@ -37,6 +37,17 @@ fe_status check_cuda(cudaError_t err, const char *what);
 // input (allocated once per device on first use).
 int *device_status_word(int device);
 int *current_device_status_word();
+// Unique id of the CUDA context current on this thread (making the current device's
+// primary context current if none is): per-device caches (the status word, scratch and
+// counter addresses, kernel attributes) record it and are set up again when it changes,
+// so that nothing set up before a cudaDeviceReset is used in the device's next context.
+// 1 when the driver cannot tell (the caches then never refresh).
+uint64_t current_context_id();
+// The work-wait limit of the kernels of one .cu file, on the current device
+// (fe_common.cuh c_wait_limit_ns); fe_set_wait_limit calls all of them.
+cudaError_t set_wait_limit_linear(uint64_t ns);
+cudaError_t set_wait_limit_attention(uint64_t ns);
+cudaError_t set_wait_limit_attention_wide(uint64_t ns);
 int current_sm_count();
 // Programmatic dependent launch for the kernels that call grid_dep_wait(): on with
 // FE_PDL=1 (read once per process), off by default.  On bge-large, Qwen3- and

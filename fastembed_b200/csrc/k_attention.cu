@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     mbar_arrive_expect_tx(&k_full[ks], KV_BYTES / 2);
                     load_tile(dst, &k_full[ks], 1, w.head, w.start + j * TK);
                     if (!(ok = wait(&v_empty[ks], par))) {
-                        (void)mbar_wait(&k_full[ks], par ^ 1);  // the K load just started lands first
+                        (void)mbar_wait_drain(&k_full[ks], par ^ 1);  // the K load just started lands first
                         break;
                     }
                     mbar_arrive_expect_tx(&v_full[ks], KV_BYTES / 2);
@@ -269,11 +269,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             }
             // every load this thread started lands before the CTA exits
             for (int i = 0; i < Q_SLOTS; ++i)
-                if ((q_armed >> i) & 1) (void)mbar_wait(&q_full[i], (q_par >> i) & 1);
+                if ((q_armed >> i) & 1) (void)mbar_wait_drain(&q_full[i], (q_par >> i) & 1);
             for (int i = 0; i < KV_SLOTS; ++i)
                 if ((kv_armed >> i) & 1) {
-                    (void)mbar_wait(&k_full[i], (kv_par >> i) & 1);
-                    (void)mbar_wait(&v_full[i], (kv_par >> i) & 1);
+                    (void)mbar_wait_drain(&k_full[i], (kv_par >> i) & 1);
+                    (void)mbar_wait_drain(&v_full[i], (kv_par >> i) & 1);
                 }
         }
     } else if (warp == 1) {
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             if (issued) {
                 // all MMAs issued by this thread retire before TMEM is released
                 umma_commit(probe);
-                (void)mbar_wait(probe, 0);
+                (void)mbar_wait_drain(probe, 0);
             }
         }
     } else {
@@ -529,14 +529,15 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
         *st = r;
         return cudaSuccess;
     }
-    static bool configured[64] = {};
+    static uint64_t configured[64] = {};  // context the attribute was set in
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev]) {
+    const uint64_t ctx = current_context_id();
+    if (dev < 64 && configured[dev] != ctx) {
         cudaError_t e = cudaFuncSetAttribute(attn_varlen_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              SMEM_BYTES);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured[dev] = ctx;
     }
     const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
     const int ctas = kCtasPerSm * current_sm_count();
@@ -544,6 +545,7 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
     // on different streams use different counters); the counters live in this module.
     static std::mutex sched_mu;
     static unsigned *sched_base[64] = {};
+    static uint64_t sched_ctx[64] = {};  // context the address was looked up in
     static unsigned next_slot[64] = {};
     if (dev >= 64) {
         *st = fail(FE_ERR_UNSUPPORTED, "attention: device index above 63");
@@ -553,11 +555,12 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
     unsigned slot = 0;
     {
         std::lock_guard<std::mutex> lock(sched_mu);
-        if (!sched_base[dev]) {
+        if (!sched_base[dev] || sched_ctx[dev] != ctx) {
             void *p = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&p, g_attn_sched);
             if (e != cudaSuccess) return e;
             sched_base[dev] = static_cast<unsigned *>(p);
+            sched_ctx[dev] = ctx;
         }
         sched_dev = sched_base[dev];
         slot = next_slot[dev];
@@ -578,4 +581,8 @@ cudaError_t launch_attention_varlen(const void *qkv, const int32_t *cu_seqlens, 
     return cudaSuccess;
 }
 
+}  // namespace fe
+
+namespace fe {
+cudaError_t set_wait_limit_attention(uint64_t ns) { return set_wait_limit_this_file(ns); }
 }  // namespace fe

@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                     t_last = globaltimer_ns();
                 } else {
                     __nanosleep(32);
-                    if ((i & 255u) == 255u && globaltimer_ns() - t_last > kWaitLimitNs) {
+                    if (((i & 255u) == 255u || wait_limit_ns() < kShortWaitNs) && globaltimer_ns() - t_last > wait_limit_ns()) {
                         report(status, DEV_TIMEOUT);
                         *abort_flag = 1;
                         ok = false;
@@ -271,10 +271,10 @@ __global__ void __launch_bounds__(kThreadsW, 1)
             }
             // every load this thread started lands before the CTA exits
             for (int i = 0; i < QS; ++i)
-                if ((q_armed >> i) & 1) (void)mbar_wait(&q_full[i], (q_par >> i) & 1);
+                if ((q_armed >> i) & 1) (void)mbar_wait_drain(&q_full[i], (q_par >> i) & 1);
             for (int i = 0; i < KVS; ++i) {
-                if ((k_armed >> i) & 1) (void)mbar_wait(&k_full[i], (k_par >> i) & 1);
-                if ((v_armed >> i) & 1) (void)mbar_wait(&v_full[i], (v_par >> i) & 1);
+                if ((k_armed >> i) & 1) (void)mbar_wait_drain(&k_full[i], (k_par >> i) & 1);
+                if ((v_armed >> i) & 1) (void)mbar_wait_drain(&v_full[i], (v_par >> i) & 1);
             }
         }
     } else if (warp == 1) {
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kThreadsW, 1)
             if (ok && have_pend && !*abort_flag) ok = issue_pv();
             if (issued) {
                 umma_commit(probe);
-                (void)mbar_wait(probe, 0);
+                (void)mbar_wait_drain(probe, 0);
             }
         }
     } else {
@@ -516,14 +516,15 @@ template <int HD>
 cudaError_t launch_wide(const CUtensorMap &tm, const int32_t *cu, int batch, int q_heads, int kv_heads, int causal,
                         float scale_log2, __nv_bfloat16 *out, int grid, cudaStream_t s)
 {
-    static bool configured[64] = {};
+    static uint64_t configured[64] = {};  // context the attribute was set in
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev]) {
+    const uint64_t ctx = current_context_id();
+    if (dev < 64 && configured[dev] != ctx) {
         cudaError_t e = cudaFuncSetAttribute(attn_wide_tcgen05<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              WCfg<HD>::SMEM);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured[dev] = ctx;
     }
     return launch_k(attn_wide_tcgen05<HD>, dim3(grid), dim3(kThreadsW), WCfg<HD>::SMEM, s, tm, cu, batch, q_heads,
                     kv_heads, causal, scale_log2, out, current_device_status_word());
@@ -561,4 +562,8 @@ cudaError_t launch_attention_wide(const void *qkv, const int32_t *cu_seqlens, in
     return cudaSuccess;
 }
 
+}  // namespace fe
+
+namespace fe {
+cudaError_t set_wait_limit_attention_wide(uint64_t ns) { return set_wait_limit_this_file(ns); }
 }  // namespace fe

@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Drain: every load this thread started must land before the CTA exits.
             for (int s = 0; s < C::STAGES; ++s)
                 if (armed & (1u << s))
-                    if (!mbar_wait(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
+                    if (!mbar_wait_drain(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Let outstanding MMAs retire before TMEM is released.
                 uint64_t *probe = &acc_full[acc];
                 umma_commit(probe);
-                if (!mbar_wait(probe, acc_phase)) report(status, DEV_TIMEOUT);
+                if (!mbar_wait_drain(probe, acc_phase)) report(status, DEV_TIMEOUT);
             }
         }
     } else {
@@ -443,7 +443,7 @@ __device__ __forceinline__ void pair_producer(uint8_t *ring, uint64_t *full, uin
     if (rank == 0)
         for (int s = 0; s < STAGES; ++s)
             if (armed & (1u << s))
-                if (!mbar_wait(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
+                if (!mbar_wait_drain(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
 }
 
 // MMA issuer of a pair (lane 0 of warp 1 in the leader): 256 x 256 x 64 per stage
@@ -497,7 +497,7 @@ __device__ __forceinline__ void pair_mma(uint8_t *ring, uint64_t *full, uint64_t
         // Let outstanding MMAs retire before TMEM is released.
         uint64_t *probe = &acc_full[acc];
         umma_commit_pair_both(probe);
-        if (!mbar_wait(probe, acc_phase)) report(status, DEV_TIMEOUT);
+        if (!mbar_wait_drain(probe, acc_phase)) report(status, DEV_TIMEOUT);
     }
 }
 
@@ -950,7 +950,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
                     pq_sum = qs;
                 }
                 if (__all_sync(0xffffffffu, ready)) break;
-                const bool stop = (it & 15u) == 15u && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs);
+                const bool stop = (it & 15u) == 15u && (*abort_flag || globaltimer_ns() - t0 > wait_limit_ns());
                 if (__any_sync(0xffffffffu, stop)) {  // the same decision in every lane
                     ok = false;
                     break;
@@ -1047,7 +1047,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
         if (lane == 0) {
             for (int b = 0; b < SLABS; ++b)
                 if (inflight & (1u << b))
-                    if (!mbar_wait(&rbar[b], (rpar >> b) & 1u)) report(status, DEV_TIMEOUT);
+                    if (!mbar_wait_drain(&rbar[b], (rpar >> b) & 1u)) report(status, DEV_TIMEOUT);
             bulk_wait_all<0>();
         }
         __syncwarp();
@@ -1073,13 +1073,14 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
 {
     using Cfg = PairCfg<kPairStages, kPairEpiWarps>;
     auto kern = linear_tcgen05_pair<OUT_BF16, kPairStages, kPairEpiWarps>;
-    static bool configured[64] = {};
+    static uint64_t configured[64] = {};  // context the attribute was set in
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev]) {
+    const uint64_t ctx = current_context_id();
+    if (dev < 64 && configured[dev] != ctx) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured[dev] = ctx;
     }
     const int tiles = ((M + 255) / 256) * ((N + P_BN - 1) / P_BN);
     int pairs = current_sm_count() / 2;
@@ -1095,9 +1096,11 @@ template <class Cfg, int STAGES, int EPI_WARPS, int SLABS>
 int ln_resident_pairs()
 {
     static int cached[64] = {};
+    static uint64_t cached_ctx[64] = {};  // context the attribute was set in
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && cached[dev] > 0) return cached[dev];
+    const uint64_t ctx = current_context_id();
+    if (dev < 64 && cached[dev] > 0 && cached_ctx[dev] == ctx) return cached[dev];
     auto kern = linear_ln_tcgen05_pair<STAGES, EPI_WARPS, SLABS>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess) return 0;
     cudaLaunchConfig_t cfg = {};
@@ -1109,7 +1112,10 @@ int ln_resident_pairs()
         cudaGetLastError();
         return 0;
     }
-    if (dev < 64) cached[dev] = clusters;
+    if (dev < 64) {
+        cached[dev] = clusters;
+        cached_ctx[dev] = ctx;
+    }
     return clusters;
 }
 
@@ -1119,14 +1125,15 @@ cudaError_t launch(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorM
                    cudaStream_t s)
 {
     using C = Cfg<BN>;
-    static bool configured[64] = {};
+    static uint64_t configured[64] = {};  // context the attribute was set in
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev]) {
+    const uint64_t ctx = current_context_id();
+    if (dev < 64 && configured[dev] != ctx) {
         cudaError_t e = cudaFuncSetAttribute(linear_tcgen05<BN, OUT_BF16>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured[dev] = ctx;
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     int grid = current_sm_count();
@@ -1210,6 +1217,7 @@ size_t round_up_256(size_t v) { return (v + 255) & ~size_t(255); }
 std::mutex g_ln_mu;
 cudaEvent_t g_ln_last[64] = {};
 cudaStream_t g_ln_last_stream[64] = {};  // stream of that launch: no wait needed on the same stream
+uint64_t g_ln_last_ctx[64] = {};          // context the event was created in
 // Next epoch of each statistics workspace (keyed by its address); 0 is never used, so
 // a zero-filled workspace holds no valid partial.
 std::unordered_map<const void *, unsigned> g_ln_epoch;
@@ -1319,7 +1327,13 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(s, &cap);
     const bool order = cap == cudaStreamCaptureStatusNone && dev < 64;
+    const uint64_t ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_ln_mu);
+    if (order && g_ln_last[dev] && g_ln_last_ctx[dev] != ctx) {
+        // the device was reset since the event was made: it and its stream are gone
+        g_ln_last[dev] = nullptr;
+        g_ln_last_stream[dev] = nullptr;
+    }
     unsigned &ep = g_ln_epoch[stats];
     if (++ep == 0) ep = 1;
     p.epoch = ep;
@@ -1337,6 +1351,7 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
         if (!g_ln_last[dev]) {
             e = cudaEventCreateWithFlags(&g_ln_last[dev], cudaEventDisableTiming);
             if (e != cudaSuccess) return e;
+            g_ln_last_ctx[dev] = ctx;
         }
         e = cudaEventRecord(g_ln_last[dev], s);
         g_ln_last_stream[dev] = s;
@@ -1344,4 +1359,8 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
     return e;
 }
 
+}  // namespace fe
+
+namespace fe {
+cudaError_t set_wait_limit_linear(uint64_t ns) { return set_wait_limit_this_file(ns); }
 }  // namespace fe

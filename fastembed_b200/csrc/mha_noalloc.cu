@@ -21,8 +21,8 @@
 //     zero, because the three projections overwrite the Q, K and V they use before
 //     anything reads them.
 //   * The first call on each device looks up the array's device address (once per
-//     device, with that device current); make that first call before any CUDA stream
-//     capture on the device.
+//     device and CUDA context, with that device current); make that first call before
+//     any CUDA stream capture on the device.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -37,10 +37,14 @@ constexpr int kMaxDevices = 64;
 // The scratch: Q | K | V, each kNoAllocMaxElems floats, in device global memory.
 static __device__ __align__(256) float g_mha_scratch[3 * kNoAllocMaxElems];
 
-// Device address of g_mha_scratch per device.  On the host the symbol name is only a
-// handle for the runtime, not a device address, so it is never passed to a kernel.
+// Device address of g_mha_scratch per device, and the CUDA context it was looked up in.
+// On the host the symbol name is only a handle for the runtime, not a device address,
+// so it is never passed to a kernel.  After a cudaDeviceReset the library image is
+// loaded again in the device's next context, possibly at another address, so the
+// address is looked up again when the context changes.
 std::mutex g_mu;
 float *g_scratch_ptr[kMaxDevices] = {};
+uint64_t g_scratch_ctx[kMaxDevices] = {};
 
 fe_status scratch_for_current_device(float **out)
 {
@@ -48,12 +52,14 @@ fe_status scratch_for_current_device(float **out)
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fe::check_cuda(e, "fe_mha_f32_noalloc: cudaGetDevice");
     if (dev < 0 || dev >= kMaxDevices) return fe::fail(FE_ERR_UNSUPPORTED, "fe_mha_f32_noalloc: device index too large");
+    const uint64_t ctx = fe::current_context_id();
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_ptr[dev]) {
+    if (!g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_mha_scratch);
         if (e != cudaSuccess) return fe::check_cuda(e, "fe_mha_f32_noalloc: cudaGetSymbolAddress");
         g_scratch_ptr[dev] = static_cast<float *>(p);
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_ptr[dev];
     return FE_OK;

@@ -19,7 +19,14 @@ thread_local std::string g_last_error;
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 int *g_status_words[kMaxDevices] = {};
+uint64_t g_status_ctx[kMaxDevices] = {};  // context each status word was allocated in
 int g_sm_count[kMaxDevices] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+CtxGetCurrentFn g_ctx_current = nullptr;
+CtxGetIdFn g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -41,23 +48,56 @@ fe_status check_cuda(cudaError_t err, const char *what)
     return fail(s, std::string(what) + ": " + cudaGetErrorName(err) + " (" + cudaGetErrorString(err) + ")");
 }
 
+uint64_t current_context_id()
+{
+    std::call_once(g_ctx_once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_id = reinterpret_cast<CtxGetIdFn>(fn);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!g_ctx_current || !g_ctx_id || g_ctx_current(&ctx) != CUDA_SUCCESS)
+        return 1;  // unknown: caches then behave as if the context never changes
+    if (!ctx) {  // no context current on this thread yet: make the device's primary context current
+        cudaFree(nullptr);
+        if (g_ctx_current(&ctx) != CUDA_SUCCESS || !ctx) return 1;
+    }
+    if (g_ctx_id(ctx, &id) != CUDA_SUCCESS) return 1;
+    return static_cast<uint64_t>(id) + 2;
+}
+
 int *device_status_word(int device)
 {
     if (device < 0 || device >= kMaxDevices) return nullptr;
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_status_words[device]) {
-        int prev = 0;
-        cudaGetDevice(&prev);
-        cudaSetDevice(device);
-        int *p = nullptr;
-        if (cudaMalloc(&p, sizeof(int)) == cudaSuccess) {
-            cudaMemset(p, 0, sizeof(int));
-            cudaDeviceSynchronize();
-            g_status_words[device] = p;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != device) cudaSetDevice(device);
+    const uint64_t ctx = current_context_id();
+    int *word = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_status_words[device] || g_status_ctx[device] != ctx) {
+            // first use on this device, or the device was reset since: the word lives in the current context
+            int *p = nullptr;
+            g_status_words[device] = nullptr;
+            if (cudaMalloc(&p, sizeof(int)) == cudaSuccess) {
+                cudaMemset(p, 0, sizeof(int));
+                cudaDeviceSynchronize();
+                g_status_words[device] = p;
+                g_status_ctx[device] = ctx;
+            }
         }
-        cudaSetDevice(prev);
+        word = g_status_words[device];
     }
-    return g_status_words[device];
+    if (prev != device) cudaSetDevice(prev);
+    return word;
 }
 
 int *current_device_status_word()
@@ -168,6 +208,23 @@ const char *fe_status_string(fe_status s)
 const char *fe_last_error_message(void) { return fe::g_last_error.c_str(); }
 
 const char *fe_version(void) { return "fastembed_b200 0.1 (sm_100a)"; }
+
+fe_status fe_set_wait_limit(int device, uint64_t limit_ns)
+{
+    if (limit_ns == 0) return fe::fail(FE_ERR_INVALID_ARGUMENT, "fe_set_wait_limit: limit_ns must be > 0");
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return fe::check_cuda(e, "fe_set_wait_limit");
+    if (device < 0 || device >= count) return fe::fail(FE_ERR_INVALID_ARGUMENT, "bad device index");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = fe::set_wait_limit_linear(limit_ns);
+    if (e == cudaSuccess) e = fe::set_wait_limit_attention(limit_ns);
+    if (e == cudaSuccess) e = fe::set_wait_limit_attention_wide(limit_ns);
+    cudaSetDevice(prev);
+    return fe::check_cuda(e, "fe_set_wait_limit");
+}
 
 fe_status fe_device_status(int device)
 {

@@ -75,8 +75,21 @@ const char *fe_status_string(fe_status s);
 /* Detail of the last failing call on this thread ("" if none). */
 const char *fe_last_error_message(void);
 /* Synchronises `device` and returns (then clears) its device-side status word:
- * FE_OK, or FE_ERR_DEVICE_TIMEOUT when a kernel's bounded wait ran out. */
+ * FE_OK, or FE_ERR_DEVICE_TIMEOUT when a kernel's bounded wait ran out.  The word and
+ * the library's other per-device state (scratch and counter addresses, kernel
+ * attributes) belong to the device's current CUDA context and are set up again in a
+ * new one: a device may be reset (cudaDeviceReset) while no call of this library is in
+ * flight on it. */
 fe_status fe_device_status(int device);
+/* Sets the limit, in nanoseconds, of the device-side waits that guard work (a TMA stage,
+ * a TMEM accumulator, another CTA's row statistics) in every tcgen05 kernel launched on
+ * `device` from now on; default 2,000,000,000 (2 s).  A wait that runs out makes its
+ * kernel record FE_ERR_DEVICE_TIMEOUT, let its own in-flight copies and MMAs land (those
+ * drain waits keep the 2 s limit), free its TMEM and return.  Limits under 1 ms are
+ * checked at every poll.  Call it with no kernel of this library running on the device.
+ * The reference has no counterpart: its CUDA ops exit() on a CUDA error
+ * (src/ops/cuda/cuda_matrix_ops.cu:13-19).  limit_ns must be > 0. */
+fe_status fe_set_wait_limit(int device, uint64_t limit_ns);
 /* Library version string. */
 const char *fe_version(void);
 
@@ -330,7 +343,11 @@ fe_status fe_engine_encode_packed(fe_engine *e, const int32_t *ids, const int32_
  * in, runs, copies out and synchronises.  Consecutive sentences run as one device
  * pass of at most FE_MAX_TOKENS_PER_PASS tokens (default 262,144; a longer sentence
  * runs alone) and 65,535 sentences, so device memory stays bounded for any batch, as
- * the reference's one-sentence-at-a-time loop does.  The token-id form of
+ * the reference's one-sentence-at-a-time loop does.  The device status word is read
+ * after every pass: a bad token id (FE_ERR_INVALID_ARGUMENT) or a wait that ran out
+ * (FE_ERR_DEVICE_TIMEOUT) ends the call before the next pass.  The word is per device,
+ * not per engine, so it also reports such an error recorded since its last read by
+ * another engine's or op's kernel on the same device.  The token-id form of
  * SentenceTransformerImpl::encode_batch (src/sentence_transformers_impl.cpp:359-365). */
 fe_status fe_engine_encode_host(fe_engine *e, const int32_t *ids, const int32_t *lengths,
                                 int32_t batch, int32_t stride, float *out);

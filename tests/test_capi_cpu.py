@@ -67,6 +67,7 @@ def test_validation_happens_before_any_device_work(fe_lib):
                                       None) == 1  # workspace too small
     # zero-sized work is a no-op
     assert L.fe_linear_bf16(None, None, None, None, None, 0, 8, 64, EPI["none"], DTYPE["bf16"], None) == 0
+    assert L.fe_set_wait_limit(0, 0) == 1  # a zero limit is refused before any device is touched
 
 
 def test_engine_create_without_gpu_fails_cleanly(fe_lib):
