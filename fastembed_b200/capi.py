@@ -103,6 +103,9 @@ _SIGS = {
     "fe_plan_shards": ([C.POINTER(EncoderConfig), vp, i32, i32, vp], C.c_int),
     "fe_plan_shards_costs": ([vp, i32, i32, vp], C.c_int),
     "fe_pack_batch": ([vp, vp, i32, i32, vp, vp], C.c_int),
+    "fe_wordpiece_create": ([C.c_char_p, C.POINTER(vp)], C.c_int),
+    "fe_wordpiece_destroy": ([vp], C.c_int),
+    "fe_wordpiece_encode": ([vp, C.c_char_p, sz, vp, sz, C.POINTER(sz)], C.c_int),
 }
 
 

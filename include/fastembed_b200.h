@@ -370,6 +370,20 @@ fe_status fe_plan_shards_costs(const double *costs, int32_t batch, int32_t parts
 fe_status fe_pack_batch(const int32_t *ids, const int32_t *lengths, int32_t batch,
                         int32_t stride, int32_t *ids_packed, int32_t *cu_seqlens);
 
+/* BGE WordPiece tokenizer, host only: replaces BGETokenizer (include/tokenizer.h:11-23;
+ * tokenize + encode, src/tokenizer.cpp:9-160).  The vocabulary is vocab.txt, one token per
+ * line, its line number the id (a repeated line keeps its last id); it must hold [UNK]
+ * (FE_ERR_IO otherwise, or when the file cannot be read). */
+typedef struct fe_wordpiece fe_wordpiece;
+fe_status fe_wordpiece_create(const char *vocab_path, fe_wordpiece **out);
+fe_status fe_wordpiece_destroy(fe_wordpiece *t);
+/* The ids of `text` (`len` bytes, any bytes) with [CLS]=101 in front and [SEP]=102
+ * behind, as SentenceTransformerImpl::tokenize frames them
+ * (src/sentence_transformers_impl.cpp:11-27).  *count receives the number of ids; at most
+ * `capacity` are written to ids (call with capacity 0 to size the buffer). */
+fe_status fe_wordpiece_encode(const fe_wordpiece *t, const char *text, size_t len, int32_t *ids,
+                              size_t capacity, size_t *count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -232,3 +232,41 @@ class Model:
         if rc != 0:
             raise ValueError(f"oracle batch forward failed with status {rc}")
         return out
+
+
+# ---------------- tokenizer ----------------
+class RefTokenizer:
+    """The reference's own BGETokenizer (oracle/_ref/libfe_ref_tok.so: src/tokenizer.cpp
+    compiled unmodified, driven by ref_tokenizer.cpp) with the [CLS] / [SEP] framing of
+    SentenceTransformerImpl::tokenize (src/sentence_transformers_impl.cpp:11-27)."""
+
+    PATH = os.path.join(HERE, "_ref", "libfe_ref_tok.so")
+
+    @classmethod
+    def available(cls) -> bool:
+        return os.path.exists(cls.PATH)
+
+    def __init__(self, vocab_path: str):
+        lib = C.CDLL(self.PATH)
+        lib.fe_ref_tok_create.argtypes = [C.c_char_p]
+        lib.fe_ref_tok_create.restype = C.c_void_p
+        lib.fe_ref_tok_destroy.argtypes = [C.c_void_p]
+        lib.fe_ref_tok_destroy.restype = None
+        lib.fe_ref_tok_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, _i32p, C.c_size_t]
+        lib.fe_ref_tok_encode.restype = C.c_long
+        self._lib = lib
+        self._h = lib.fe_ref_tok_create(vocab_path.encode())
+        if not self._h:
+            raise ValueError(f"the reference tokenizer rejected {vocab_path}")
+
+    def encode(self, text: bytes) -> list[int]:
+        buf = np.empty(4 * len(text) + 8, np.int32)
+        n = self._lib.fe_ref_tok_encode(self._h, text, len(text), buf, buf.size)
+        if n < 0 or n > buf.size:
+            raise ValueError("the reference tokenizer failed")
+        return buf[:n].tolist()
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.fe_ref_tok_destroy(self._h)
+            self._h = None
