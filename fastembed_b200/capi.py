@@ -88,6 +88,8 @@ _SIGS = {
     "fe_rms_norm_rows": ([vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),
     "fe_rms_sandwich": ([vp, vp, vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),
     "fe_rms_sandwich_bf16": ([vp, vp, vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),
+    "fe_linear_qk_norm_rope_bf16": ([vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, f32, f32, vp], C.c_int),
+    "fe_token_positions": ([vp, i32, vp, vp], C.c_int),
     "fe_qk_norm_rope_bf16": ([vp, vp, i32, i64, i32, i32, i32, vp, vp, i32, f32, f32, vp], C.c_int),
     "fe_pool_l2": ([vp, vp, i32, i32, C.c_int, vp, vp], C.c_int),
     "fe_engine_create": ([C.POINTER(EncoderConfig), C.c_int, C.POINTER(vp)], C.c_int),

@@ -388,6 +388,43 @@ fe_status fe_qk_norm_rope_bf16(void *qkv, const int32_t *cu_seqlens, int32_t bat
                 "fe_qk_norm_rope_bf16");
 }
 
+fe_status fe_linear_qk_norm_rope_bf16(const void *x, const void *w, const float *q_w, const float *k_w,
+                                      const int32_t *positions, void *qkv, int64_t m, int64_t k, int32_t q_heads,
+                                      int32_t kv_heads, int32_t head_dim, int32_t one_plus, float eps, float theta,
+                                      fe_stream_t stream)
+{
+    if (m < 0 || k <= 0 || q_heads <= 0 || kv_heads <= 0 || !(theta > 1.0f))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: bad shape");
+    if (k % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: k must be a multiple of 8");
+    if (head_dim != 128 && head_dim != 256)
+        return fail(FE_ERR_UNSUPPORTED, "fe_linear_qk_norm_rope_bf16: head_dim must be 128 or 256");
+    if ((static_cast<int64_t>(q_heads) * head_dim) % 256 != 0 || (static_cast<int64_t>(kv_heads) * head_dim) % 256 != 0)
+        return fail(FE_ERR_UNSUPPORTED,
+                    "fe_linear_qk_norm_rope_bf16: q_heads * head_dim and kv_heads * head_dim must be multiples of 256");
+    if (m > 0x7fffffff || k > 0x7fffffff || static_cast<int64_t>(q_heads + 2 * kv_heads) * head_dim > 0x7fffffff)
+        return fail(FE_ERR_UNSUPPORTED, "fe_linear_qk_norm_rope_bf16: size too large");
+    if (m == 0) return FE_OK;
+    if (!x || !w || !q_w || !k_w || !positions || !qkv)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: null pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(qkv))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: pointers must be 16-byte aligned");
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_linear_qk_norm_rope(x, w, qkv, m, k, q_heads, kv_heads, head_dim, q_w, k_w, positions,
+                                                   one_plus != 0, eps, theta, reinterpret_cast<cudaStream_t>(stream),
+                                                   &st);
+    if (st != FE_OK) return st;
+    return done(e, "fe_linear_qk_norm_rope_bf16");
+}
+
+fe_status fe_token_positions(const int32_t *cu_seqlens, int32_t batch, int32_t *positions, fe_stream_t stream)
+{
+    if (batch < 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_token_positions: bad batch");
+    if (batch == 0) return FE_OK;
+    if (!cu_seqlens || !positions) return fail(FE_ERR_INVALID_ARGUMENT, "fe_token_positions: null pointer");
+    return done(fe::launch_token_positions(cu_seqlens, batch, positions, reinterpret_cast<cudaStream_t>(stream)),
+                "fe_token_positions");
+}
+
 fe_status fe_pool_l2(const float *h, const int32_t *cu_seqlens, int32_t batch, int32_t dim, fe_pooling mode,
                      float *out, fe_stream_t stream)
 {

@@ -411,6 +411,15 @@ fe_status ensure_activations_rms(fe_engine *e, int64_t T)
     return FE_OK;
 }
 
+bool qkrope_fuse_enabled()
+{
+    static const bool on = [] {
+        const char *v = getenv("FE_QKROPE_FUSE");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 // Theta of layer l (Gemma3: every full_attention_every-th layer is a global layer).
 float layer_theta(const fe_rms_encoder_config &c, int l)
 {
@@ -489,11 +498,25 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
                                              nullptr, x16, s));
     }
     float *fin = e->hfin.as<float>();  // the final-norm output (fp32) for pooling
+    // The q/k norms and RoPE run in the QKV projection's epilogue when every head group
+    // starts on a 256-column tile (FE_QKROPE_FUSE=0: the separate row kernel, for comparison)
+    const bool fuse_rope = qkrope_fuse_enabled() && (static_cast<int64_t>(c.q_heads) * hd) % 256 == 0 &&
+                           (static_cast<int64_t>(c.kv_heads) * hd) % 256 == 0;
     for (int l = 0; l < c.layers; ++l) {
         const RLayer &L = e->rlayers[l];
         const bool last = l + 1 == c.layers;
-        FE_TRY(gemm(x16, L.wqkv, nullptr, nullptr, qkv, QKV, D, FE_EPI_NONE, FE_DTYPE_BF16));
-        {
+        if (fuse_rope) {
+            // QKV projection with the q/k norms and RoPE in its epilogue
+            Scope sc(e, CAT_GEMM, s);
+            fe_status st = FE_OK;
+            cudaError_t err = fe::launch_linear_qk_norm_rope(x16, L.wqkv.p, qkv, T, D, c.q_heads, c.kv_heads,
+                                                             static_cast<int>(hd), L.q_norm.as<float>(),
+                                                             L.k_norm.as<float>(), e->tpos.as<int32_t>(), gemma, eps,
+                                                             layer_theta(c, l), s, &st);
+            if (st != FE_OK) return st;
+            FE_TRY_CUDA(err);
+        } else {
+            FE_TRY(gemm(x16, L.wqkv, nullptr, nullptr, qkv, QKV, D, FE_EPI_NONE, FE_DTYPE_BF16));
             Scope sc(e, CAT_OTHER, s);
             FE_TRY_CUDA(fe::launch_qk_norm_rope(qkv, cu, batch, T, c.q_heads, c.kv_heads, static_cast<int>(hd),
                                                 L.q_norm.as<float>(), L.k_norm.as<float>(), gemma, eps,

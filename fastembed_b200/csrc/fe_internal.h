@@ -73,6 +73,14 @@ fe_status make_tmap_heads(CUtensorMap *map, const void *base, uint64_t heads, ui
 cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
                                const float *residual, void *y, int64_t m, int64_t n, int64_t k,
                                int epilogue, int y_dtype, cudaStream_t s, fe_status *st);
+// QKV projection y = x W^T [m, (q_heads + 2 kv_heads) * head_dim] in bf16, no bias, with the
+// per-head RMSNorm (w, or 1 + w when one_plus) and rotate-half RoPE (positions pos[m], base
+// theta) of the query and key heads applied in the GEMM epilogue; value heads as they are.
+// Needs (q_heads * head_dim) % 256 == 0 and (kv_heads * head_dim) % 256 == 0 (not checked).
+cudaError_t launch_linear_qk_norm_rope(const void *x, const void *w, void *y, int64_t m, int64_t k, int q_heads,
+                                       int kv_heads, int head_dim, const float *q_w, const float *k_w,
+                                       const int32_t *pos, bool one_plus, float eps, float theta, cudaStream_t s,
+                                       fe_status *st);
 // h32 <- LayerNorm((x W^T + bias) + h32) * gamma + beta; h16 <- bf16 of it (h16 may be
 // null).  stats / y_fallback come from linear_layernorm_split_workspace; the stats
 // region must be zero-filled before its first launch.

@@ -37,7 +37,10 @@ constexpr int kEpiWarps = 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, mma, 4 epilogue warps
 constexpr uint32_t kStageBufBytes = 32 * 128;  // one warp's 32-row x 128 B store slab
 
-enum Epi : int { E_NONE = 0, E_BIAS = 1, E_GELU = 2, E_RELU = 3, E_SWISH = 4, E_RESID = 5, E_SWIGLU = 6, E_GEGLU = 7 };
+enum Epi : int {
+    E_NONE = 0, E_BIAS = 1, E_GELU = 2, E_RELU = 3, E_SWISH = 4, E_RESID = 5, E_SWIGLU = 6, E_GEGLU = 7,
+    E_QKROPE = 8  // per-head q/k RMSNorm + rotary embedding of a QKV projection (RopeParams)
+};
 
 template <int BN>
 struct Cfg {
@@ -60,6 +63,98 @@ __device__ __forceinline__ float act(float x, int epi)
     return x;
 }
 
+// Per-head RMSNorm of the query and key heads followed by the rotate-half rotary embedding,
+// applied to a QKV projection's accumulator before it is rounded to bf16 (E_QKROPE): the
+// Qwen3 / Gemma3 q_norm / k_norm and RoPE, which otherwise run as a separate pass over the
+// bf16 qkv buffer.  Columns [0, q_cols) are query heads, [q_cols, k_end) key heads, the
+// rest value heads (stored as they are); every head-group boundary falls on a 256-column
+// tile boundary, so a tile is all query, all key or all value.
+struct RopeParams {
+    const int32_t *pos;    // [M] position of each row's token in its sentence
+    const float *qw, *kw;  // [hd] q_norm / k_norm weights
+    int q_cols, k_end;
+    int hd;                // 128 or 256
+    int one_plus;          // Gemma3 weight form (1 + w)
+    float eps, log2_theta;
+};
+
+// One warp's 32 rows x BN columns of a query or key tile: for each head, pass 1 sums
+// the squares of its HD accumulator columns (a thread owns a row, so no shuffles), pass 2
+// reads each element with its rotation partner HD/2 columns away, normalises both, rotates
+// them and stages them in the two 128-byte slabs (columns lo and lo + HD/2) that are
+// TMA-stored together.  Leaves no store reading shared memory.
+template <int BN, int HD>
+__device__ __forceinline__ void drain_qk_rope(uint32_t t_row, int row, int store_row, int n0, int M,
+                                              const RopeParams &rp, const CUtensorMap *tm_y, uint8_t *bufs, int lane)
+{
+    static_assert(BN % HD == 0, "a tile holds whole heads");
+    const float *wv = n0 < rp.q_cols ? rp.qw : rp.kw;
+    const float wadd = rp.one_plus ? 1.f : 0.f;
+    const int pos = row < M ? __ldg(rp.pos + row) : 0;
+    uint8_t *buf_lo = bufs, *buf_hi = bufs + kStageBufBytes;
+#pragma unroll 1
+    for (int h0 = 0; h0 < BN; h0 += HD) {
+        float ss = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+            uint32_t v[32];
+            tmem_ld_x32(t_row + h0 + c, v);
+            tmem_wait_ld_regs(v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(v[j]), __uint_as_float(v[j]), ss);
+        }
+        const float r = rsqrtf(ss / static_cast<float>(HD) + rp.eps);
+#pragma unroll 1
+        for (int sl = 0; sl < HD / 128; ++sl) {
+            if (lane == 0) bulk_wait_read<0>();  // the slabs' previous stores have read shared memory
+            __syncwarp();
+            uint8_t *pa = buf_lo + lane * 128, *pb = buf_hi + lane * 128;
+#pragma unroll 1
+            for (int cc = 0; cc < 2; ++cc) {
+                const int lo = 64 * sl + 32 * cc;  // head column of this chunk's first element
+                uint32_t a[32], b[32];
+                tmem_ld_x32(t_row + h0 + lo, a);
+                tmem_ld_x32(t_row + h0 + lo + HD / 2, b);
+                tmem_wait_ld_regs(a);
+                tmem_wait_ld_regs(b);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float sn, cs;
+                    rope_angle<HD>(pos, lo + j, rp.log2_theta, sn, cs);
+                    const float xa = __uint_as_float(a[j]) * r * (__ldg(wv + lo + j) + wadd);
+                    const float xb = __uint_as_float(b[j]) * r * (__ldg(wv + lo + j + HD / 2) + wadd);
+                    a[j] = __float_as_uint(xa * cs - xb * sn);
+                    b[j] = __float_as_uint(xb * cs + xa * sn);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {  // 32 bf16 = 16-byte units 4 cc .. 4 cc + 3 of the slab row
+                    const int c16 = 4 * cc + u;
+                    uint4 wa, wb;
+                    wa.x = pack_bf16x2(__uint_as_float(a[8 * u + 0]), __uint_as_float(a[8 * u + 1]));
+                    wa.y = pack_bf16x2(__uint_as_float(a[8 * u + 2]), __uint_as_float(a[8 * u + 3]));
+                    wa.z = pack_bf16x2(__uint_as_float(a[8 * u + 4]), __uint_as_float(a[8 * u + 5]));
+                    wa.w = pack_bf16x2(__uint_as_float(a[8 * u + 6]), __uint_as_float(a[8 * u + 7]));
+                    wb.x = pack_bf16x2(__uint_as_float(b[8 * u + 0]), __uint_as_float(b[8 * u + 1]));
+                    wb.y = pack_bf16x2(__uint_as_float(b[8 * u + 2]), __uint_as_float(b[8 * u + 3]));
+                    wb.z = pack_bf16x2(__uint_as_float(b[8 * u + 4]), __uint_as_float(b[8 * u + 5]));
+                    wb.w = pack_bf16x2(__uint_as_float(b[8 * u + 6]), __uint_as_float(b[8 * u + 7]));
+                    *reinterpret_cast<uint4 *>(pa + ((c16 ^ (lane & 7)) << 4)) = wa;
+                    *reinterpret_cast<uint4 *>(pb + ((c16 ^ (lane & 7)) << 4)) = wb;
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(tm_y, buf_lo, n0 + h0 + 64 * sl, store_row);
+                tma_store_2d(tm_y, buf_hi, n0 + h0 + 64 * sl + HD / 2, store_row);
+                bulk_commit();
+            }
+        }
+    }
+    if (lane == 0) bulk_wait_read<0>();  // the caller's double-buffering assumes no store of these slabs pending
+    __syncwarp();
+}
+
 // Drains one 128-row x BN accumulator from TMEM (this warp's 32 lanes = 32 rows):
 // bias / activation / residual epilogue, then 32-row x 128-byte slabs staged in
 // 128B-swizzled shared memory and written by TMA (rows >= M and columns >= N are
@@ -69,9 +164,20 @@ template <int BN, bool OUT_BF16>
 __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int store_row, int n0, int M, int N,
                                                   const float *__restrict__ bias,
                                                   const float *__restrict__ residual, int epi,
-                                                  const CUtensorMap *tm_y, uint8_t *bufs, int &pp, int lane)
+                                                  const CUtensorMap *tm_y, uint8_t *bufs, int &pp, int lane,
+                                                  const RopeParams &rp)
 {
     if constexpr (OUT_BF16) {
+        if (epi == E_QKROPE) {
+            if constexpr (BN >= 256) {
+                if (n0 < rp.k_end) {
+                    if (rp.hd == 128) drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, tm_y, bufs, lane);
+                    else drain_qk_rope<BN, 256>(t_row, row, store_row, n0, M, rp, tm_y, bufs, lane);
+                    return;
+                }
+            }
+            epi = E_NONE;  // value heads: stored as they are
+        }
         if (epi == E_SWIGLU || epi == E_GEGLU) {
             // Gated MLP: W rows interleave 32 gate and 32 up rows, so each 64-column block of
             // the accumulator gives 32 outputs act(gate) * up; 128 accumulator columns fill one
@@ -209,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     linear_tcgen05(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_y, int M, int N, int K,
                    const float *__restrict__ bias, const float *__restrict__ residual, int epi,
-                   int *status)
+                   int *status, const RopeParams rp)
 {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -360,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = m0 + q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
             drain_accumulator<BN, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
-                                            lane);
+                                            lane, rp);
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
             acc ^= 1;
@@ -505,7 +611,8 @@ template <bool OUT_BF16, int P_STAGES, int EPI_WARPS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EPI_WARPS>::THREADS, 1)
     linear_tcgen05_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_y, int M, int N, int K,
-                        const float *__restrict__ bias, const float *__restrict__ residual, int epi, int *status)
+                        const float *__restrict__ bias, const float *__restrict__ residual, int epi, int *status,
+                        const RopeParams rp)
 {
     using Cfg = PairCfg<P_STAGES, EPI_WARPS>;
     extern __shared__ uint8_t smem_raw[];
@@ -588,7 +695,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
             const int row = m0 + q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN + h * COLS;
             drain_accumulator<COLS, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
-                                              lane);
+                                              lane, rp);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(leader_acc_empty[acc]);
@@ -1069,7 +1176,8 @@ constexpr int kPairEpiWarps = 4;
 
 template <bool OUT_BF16>
 cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N, int K,
-                        const float *bias, const float *residual, int epi, int *status, cudaStream_t s)
+                        const float *bias, const float *residual, int epi, int *status, cudaStream_t s,
+                        const RopeParams &rp)
 {
     using Cfg = PairCfg<kPairStages, kPairEpiWarps>;
     auto kern = linear_tcgen05_pair<OUT_BF16, kPairStages, kPairEpiWarps>;
@@ -1087,7 +1195,7 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
     if (pairs > tiles) pairs = tiles;
     if (pairs < 1) pairs = 1;
     return launch_k(kern, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, s, tx, tw, ty, M, N, K, bias, residual,
-                    epi, status);
+                    epi, status, rp);
 }
 
 // Pairs of linear_ln_tcgen05_pair<Cfg> that can be resident at once on the current
@@ -1122,7 +1230,7 @@ int ln_resident_pairs()
 template <int BN, bool OUT_BF16>
 cudaError_t launch(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N,
                    int K, const float *bias, const float *residual, int epi, int *status,
-                   cudaStream_t s)
+                   cudaStream_t s, const RopeParams &rp)
 {
     using C = Cfg<BN>;
     static uint64_t configured[64] = {};  // context the attribute was set in
@@ -1140,7 +1248,7 @@ cudaError_t launch(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorM
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
     return launch_k(linear_tcgen05<BN, OUT_BF16>, dim3(grid), dim3(kThreads), C::SMEM_BYTES, s, tx, tw, ty, M, N, K,
-                    bias, residual, epi, status);
+                    bias, residual, epi, status, rp);
 }
 
 // The 2-CTA kernel is the default for large M; FE_LINEAR_PAIR=0 selects the 1-CTA
@@ -1161,9 +1269,10 @@ bool norm_fuse_enabled()
 
 }  // namespace
 
-cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
-                               const float *residual, void *y, int64_t m, int64_t n, int64_t k,
-                               int epilogue, int y_dtype, cudaStream_t s, fe_status *st)
+namespace {
+cudaError_t launch_linear_any(const void *x, const void *w, const float *bias, const float *residual, void *y,
+                              int64_t m, int64_t n, int64_t k, int epilogue, int y_dtype, cudaStream_t s, fe_status *st,
+                              const RopeParams &rp)
 {
     *st = FE_OK;
     if (m == 0 || n == 0) return cudaSuccess;
@@ -1192,14 +1301,40 @@ cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
             *st = r;
             return cudaSuccess;
         }
-        return out_bf16 ? launch_pair<true>(tx, tw2, ty, M, N, K, bias, residual, epilogue, status, s)
-                        : launch_pair<false>(tx, tw2, ty, M, N, K, bias, residual, epilogue, status, s);
+        return out_bf16 ? launch_pair<true>(tx, tw2, ty, M, N, K, bias, residual, epilogue, status, s, rp)
+                        : launch_pair<false>(tx, tw2, ty, M, N, K, bias, residual, epilogue, status, s, rp);
     }
     if (BN == 256)
-        return out_bf16 ? launch<256, true>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s)
-                        : launch<256, false>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s);
-    return out_bf16 ? launch<128, true>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s)
-                    : launch<128, false>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s);
+        return out_bf16 ? launch<256, true>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s, rp)
+                        : launch<256, false>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s, rp);
+    return out_bf16 ? launch<128, true>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s, rp)
+                    : launch<128, false>(tx, tw, ty, M, N, K, bias, residual, epilogue, status, s, rp);
+}
+}  // namespace
+
+cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
+                               int64_t m, int64_t n, int64_t k, int epilogue, int y_dtype, cudaStream_t s, fe_status *st)
+{
+    return launch_linear_any(x, w, bias, residual, y, m, n, k, epilogue, y_dtype, s, st, RopeParams{});
+}
+
+cudaError_t launch_linear_qk_norm_rope(const void *x, const void *w, void *y, int64_t m, int64_t k, int q_heads,
+                                       int kv_heads, int head_dim, const float *q_w, const float *k_w,
+                                       const int32_t *pos, bool one_plus, float eps, float theta, cudaStream_t s,
+                                       fe_status *st)
+{
+    RopeParams rp;
+    rp.pos = pos;
+    rp.qw = q_w;
+    rp.kw = k_w;
+    rp.q_cols = q_heads * head_dim;
+    rp.k_end = (q_heads + kv_heads) * head_dim;
+    rp.hd = head_dim;
+    rp.one_plus = one_plus ? 1 : 0;
+    rp.eps = eps;
+    rp.log2_theta = log2f(theta);
+    const int64_t n = static_cast<int64_t>(q_heads + 2 * kv_heads) * head_dim;
+    return launch_linear_any(x, w, nullptr, nullptr, y, m, n, k, E_QKROPE, FE_DTYPE_BF16, s, st, rp);
 }
 
 }  // namespace fe

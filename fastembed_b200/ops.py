@@ -214,6 +214,27 @@ def qk_norm_rope(qkv, cu_seqlens, q_heads, kv_heads, head_dim, q_w, k_w, eps, th
     return qkv
 
 
+def token_positions(cu_seqlens):
+    """int32 [T]: each token's position in its sentence."""
+    _cuda(cu_seqlens)
+    B = cu_seqlens.numel() - 1
+    T = int(cu_seqlens[-1].item()) if B > 0 else 0
+    pos = torch.empty(max(T, 1), dtype=torch.int32, device=cu_seqlens.device)
+    call("fe_token_positions", _p(cu_seqlens), B, _p(pos), _s(cu_seqlens))
+    return pos[:T]
+
+
+def linear_qk_norm_rope(x, w, q_w, k_w, positions, q_heads, kv_heads, head_dim, eps, theta, one_plus=False):
+    """QKV projection [m, (Hq + 2 Hkv) hd] bf16 = x @ w.T with the q/k RMSNorm and RoPE fused
+    into the GEMM epilogue."""
+    _cuda(x, w, q_w, k_w, positions)
+    m, k = x.shape
+    y = torch.empty(m, (q_heads + 2 * kv_heads) * head_dim, dtype=torch.bfloat16, device=x.device)
+    call("fe_linear_qk_norm_rope_bf16", _p(x), _p(w), _p(q_w), _p(k_w), _p(positions), _p(y), m, k, q_heads,
+         kv_heads, head_dim, 1 if one_plus else 0, eps, theta, _s(x))
+    return y
+
+
 def pool_l2(h, cu_seqlens, mode="cls"):
     _cuda(h, cu_seqlens)
     B = cu_seqlens.numel() - 1

@@ -239,6 +239,22 @@ fe_status fe_rms_sandwich_bf16(const void *y, const float *w_post, float *h32, c
                                fe_stream_t stream);
 fe_status fe_rms_sandwich(const float *y, const float *w_post, float *h32, const float *w_next, int32_t one_plus,
                           float eps, int64_t rows, int32_t dim, float *o32, void *o16, fe_stream_t stream);
+/* The Qwen3 / Gemma3 QKV projection with its q/k norms and RoPE fused into the GEMM
+ * epilogue: qkv [m, (q_heads + 2 kv_heads) * head_dim] bf16 = x [m, k] W^T ([N, k] bf16,
+ * query | key | value rows, no bias), where each query and key head is RMS-normalised in
+ * fp32 straight from the accumulator (weights q_w / k_w, or 1 + w when one_plus), then
+ * rotated (rotate-half RoPE, inverse frequencies theta^(-2i/head_dim), position
+ * positions[row]) before the single bf16 rounding; value heads are stored as they are.
+ * Replaces fe_linear_bf16 followed by fe_qk_norm_rope_bf16 (one pass over qkv fewer).
+ * head_dim 128 or 256; q_heads * head_dim and kv_heads * head_dim multiples of 256
+ * (FE_ERR_UNSUPPORTED otherwise).  Not in the reference (no Qwen3 / Gemma forward). */
+fe_status fe_linear_qk_norm_rope_bf16(const void *x, const void *w, const float *q_w, const float *k_w,
+                                      const int32_t *positions, void *qkv, int64_t m, int64_t k, int32_t q_heads,
+                                      int32_t kv_heads, int32_t head_dim, int32_t one_plus, float eps, float theta,
+                                      fe_stream_t stream);
+/* positions[t] = position of token t in its sentence (0, 1, ...) for the packed batch of
+ * cu_seqlens [batch + 1]: the positions fe_linear_qk_norm_rope_bf16 reads. */
+fe_status fe_token_positions(const int32_t *cu_seqlens, int32_t batch, int32_t *positions, fe_stream_t stream);
 /* In place on qkv [total, (q_heads + 2*kv_heads)*head_dim] bf16: per-head RMSNorm of the
  * query (q_w) and key (k_w) heads, then the rotate-half rotary embedding with inverse
  * frequencies theta^(-2i/head_dim) at positions 0.. within each sentence.  head_dim 128 / 256. */

@@ -572,3 +572,51 @@ def test_embed_scale_exact(cuda_dev):
     ids = torch.randint(0, 5000, (1234,), device=cuda_dev, generator=g, dtype=torch.int32)
     h = ops.embed_scale(ids, word, 27.712812)
     assert torch.equal(h, word[ids.long()] * torch.tensor(27.712812, device=cuda_dev))
+
+
+@pytest.mark.parametrize("pair", [True, False])
+@pytest.mark.parametrize("hd,hq,hkv,theta,one_plus", [(128, 16, 8, 1e6, False), (128, 4, 2, 1e6, False),
+                                                       (256, 3, 1, 1e4, True), (256, 3, 1, 1e6, True)])
+def test_linear_qk_norm_rope(cuda_dev, monkeypatch, pair, hd, hq, hkv, theta, one_plus):
+    """The QKV projection with the q/k RMSNorm and RoPE in its epilogue against a torch
+    fp32 reference of the same steps (fp32 product of the bf16 inputs, per-head RMSNorm,
+    rotate-half RoPE); lengths cover one token, tile edges (128 / 129 rows) and a long
+    sentence; the 2-CTA kernel (m >= 512) and the 1-CTA kernel (FE_LINEAR_PAIR=0)."""
+    from fastembed_b200 import ops
+    if not pair:
+        monkeypatch.setenv("FE_LINEAR_PAIR", "0")
+    g = torch.Generator(device=cuda_dev).manual_seed(hd + hq + int(pair))
+    lens = [1, 128, 129, 7, 600]
+    T = sum(lens)
+    D = 768 if hd == 256 else 1024
+    N = (hq + 2 * hkv) * hd
+    x = torch.randn(T, D, device=cuda_dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, D, device=cuda_dev, generator=g) * 0.05).to(torch.bfloat16)
+    qw = torch.randn(hd, device=cuda_dev, generator=g) * 0.3 + (0 if one_plus else 1)
+    kw = torch.randn(hd, device=cuda_dev, generator=g) * 0.3 + (0 if one_plus else 1)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    pos = ops.token_positions(cu)
+    assert torch.equal(pos.long(), torch.cat([torch.arange(L, device=cuda_dev) for L in lens]))
+    y = ops.linear_qk_norm_rope(x, w, qw, kw, pos, hq, hkv, hd, 1e-6, theta, one_plus).float()
+    torch.cuda.synchronize()
+    src = x.float() @ w.float().t()
+    q = src[:, :hq * hd].view(T, hq, hd)
+    k = src[:, hq * hd:(hq + hkv) * hd].view(T, hkv, hd)
+    q_ref = _rope_ref(_rms_ref(q, qw, 1e-6, one_plus), pos.long(), theta).reshape(T, -1)
+    k_ref = _rope_ref(_rms_ref(k, kw, 1e-6, one_plus), pos.long(), theta).reshape(T, -1)
+    v_ref = src[:, (hq + hkv) * hd:]
+    scale = float(max(q_ref.abs().max(), k_ref.abs().max()))
+    # one bf16 rounding of the result (2^-8 relative) plus the fp32 accumulation order
+    assert float((y[:, :hq * hd] - q_ref).abs().max()) < 1e-2 * scale
+    assert float((y[:, hq * hd:(hq + hkv) * hd] - k_ref).abs().max()) < 1e-2 * scale
+    assert float((y[:, (hq + hkv) * hd:] - v_ref).abs().max()) < 1e-2 * float(v_ref.abs().max())
+    ops.device_status(0)
+
+
+def test_linear_qk_norm_rope_rejects_unaligned_heads(cuda_dev):
+    import ctypes as C
+    from fastembed_b200 import capi
+    buf = C.c_void_p(256)
+    # 3 query heads of 128 columns do not fill whole 256-column tiles
+    st = capi.lib().fe_linear_qk_norm_rope_bf16(buf, buf, buf, buf, buf, buf, 16, 64, 3, 1, 128, 0, 1e-6, 1e6, None)
+    assert st == 4  # FE_ERR_UNSUPPORTED
