@@ -36,6 +36,7 @@ constexpr int BK = 64;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, mma, 4 epilogue warps
 constexpr uint32_t kStageBufBytes = 32 * 128;  // one warp's 32-row x 128 B store slab
+constexpr uint32_t kRopeTabBytes = 128 * 4;     // inverse RoPE frequencies of the q/k epilogue (head_dim / 2)
 
 enum Epi : int {
     E_NONE = 0, E_BIAS = 1, E_GELU = 2, E_RELU = 3, E_SWISH = 4, E_RESID = 5, E_SWIGLU = 6, E_GEGLU = 7,
@@ -52,7 +53,7 @@ struct Cfg {
     static constexpr uint32_t RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr uint32_t EPI_BYTES = kEpiWarps * 2 * kStageBufBytes;
     static constexpr uint32_t BAR_BYTES = 256;
-    static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES;
+    static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES + kRopeTabBytes;
 };
 
 __device__ __forceinline__ float act(float x, int epi)
@@ -78,6 +79,16 @@ struct RopeParams {
     float eps, log2_theta;
 };
 
+// The epilogue warps (threads 64 .. 64 + nthreads of the CTA) fill the CTA's table of
+// inverse RoPE frequencies theta^(-2i / hd), i < hd / 2, then meet at named barrier 1.
+__device__ __forceinline__ void fill_rope_table(float *inv_tab, const RopeParams &rp, int nthreads)
+{
+    const int et = static_cast<int>(threadIdx.x) - 64;
+    for (int i = et; i < rp.hd / 2; i += nthreads)
+        inv_tab[i] = exp2f(-rp.log2_theta * static_cast<float>(2 * i) / static_cast<float>(rp.hd));
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
 // One warp's 32 rows x BN columns of a query or key tile: for each head, pass 1 sums
 // the squares of its HD accumulator columns (a thread owns a row, so no shuffles), pass 2
 // reads each element with its rotation partner HD/2 columns away, normalises both, rotates
@@ -85,24 +96,31 @@ struct RopeParams {
 // TMA-stored together.  Leaves no store reading shared memory.
 template <int BN, int HD>
 __device__ __forceinline__ void drain_qk_rope(uint32_t t_row, int row, int store_row, int n0, int M,
-                                              const RopeParams &rp, const CUtensorMap *tm_y, uint8_t *bufs, int lane)
+                                              const RopeParams &rp, const float *inv_tab, const CUtensorMap *tm_y,
+                                              uint8_t *bufs, int lane)
 {
     static_assert(BN % HD == 0, "a tile holds whole heads");
     const float *wv = n0 < rp.q_cols ? rp.qw : rp.kw;
     const float wadd = rp.one_plus ? 1.f : 0.f;
-    const int pos = row < M ? __ldg(rp.pos + row) : 0;
+    const float fpos = static_cast<float>(row < M ? __ldg(rp.pos + row) : 0);
     uint8_t *buf_lo = bufs, *buf_hi = bufs + kStageBufBytes;
 #pragma unroll 1
     for (int h0 = 0; h0 < BN; h0 += HD) {
-        float ss = 0.f;
+        float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-            uint32_t v[32];
+        for (int c = 0; c < HD; c += 64) {  // two 32-column loads per wait
+            uint32_t v[32], u[32];
             tmem_ld_x32(t_row + h0 + c, v);
+            tmem_ld_x32(t_row + h0 + c + 32, u);
             tmem_wait_ld_regs(v);
+            tmem_wait_ld_regs(u);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(v[j]), __uint_as_float(v[j]), ss);
+            for (int j = 0; j < 32; ++j) {
+                ss0 = fmaf(__uint_as_float(v[j]), __uint_as_float(v[j]), ss0);
+                ss1 = fmaf(__uint_as_float(u[j]), __uint_as_float(u[j]), ss1);
+            }
         }
+        const float ss = ss0 + ss1;
         const float r = rsqrtf(ss / static_cast<float>(HD) + rp.eps);
 #pragma unroll 1
         for (int sl = 0; sl < HD / 128; ++sl) {
@@ -120,7 +138,7 @@ __device__ __forceinline__ void drain_qk_rope(uint32_t t_row, int row, int store
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     float sn, cs;
-                    rope_angle<HD>(pos, lo + j, rp.log2_theta, sn, cs);
+                    sincos_reduced(fpos * inv_tab[lo + j], sn, cs);
                     const float xa = __uint_as_float(a[j]) * r * (__ldg(wv + lo + j) + wadd);
                     const float xb = __uint_as_float(b[j]) * r * (__ldg(wv + lo + j + HD / 2) + wadd);
                     a[j] = __float_as_uint(xa * cs - xb * sn);
@@ -165,14 +183,14 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
                                                   const float *__restrict__ bias,
                                                   const float *__restrict__ residual, int epi,
                                                   const CUtensorMap *tm_y, uint8_t *bufs, int &pp, int lane,
-                                                  const RopeParams &rp)
+                                                  const RopeParams &rp, const float *inv_tab)
 {
     if constexpr (OUT_BF16) {
         if (epi == E_QKROPE) {
             if constexpr (BN >= 256) {
                 if (n0 < rp.k_end) {
-                    if (rp.hd == 128) drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, tm_y, bufs, lane);
-                    else drain_qk_rope<BN, 256>(t_row, row, store_row, n0, M, rp, tm_y, bufs, lane);
+                    if (rp.hd == 128) drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
+                    else drain_qk_rope<BN, 256>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
                     return;
                 }
             }
@@ -328,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *acc_empty = acc_full + 2;      // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *inv_tab = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(full) + C::BAR_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -448,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        if (epi == E_QKROPE) fill_rope_table(inv_tab, rp, 32 * kEpiWarps);
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         uint8_t *bufs = epi_buf + q * 2 * kStageBufBytes;
         int acc = 0;
@@ -466,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = m0 + q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
             drain_accumulator<BN, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
-                                            lane, rp);
+                                            lane, rp, inv_tab);
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
             acc ^= 1;
@@ -507,7 +527,7 @@ struct PairCfg {
     static constexpr int COLS = P_BN / (EPI_WARPS / 4);
     static constexpr uint32_t RING = STAGES * P_STAGE_BYTES;
     static constexpr uint32_t EPI = EPI_WARPS * 2 * kStageBufBytes;
-    static constexpr uint32_t SMEM = 1024 + RING + EPI + 256;
+    static constexpr uint32_t SMEM = 1024 + RING + EPI + 256 + kRopeTabBytes;
     static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "epilogue warps");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
@@ -625,6 +645,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
     uint64_t *acc_empty = acc_full + 2;                                    // used in the leader [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *inv_tab = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(full) + 256);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -675,6 +696,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
         // ---------------- epilogue (warps 2.. of both CTAs): warp w drains TMEM lanes
         // 32 * (w % 4) (the lane-quarter rule), columns [h * COLS, (h + 1) * COLS), h = (w - 2) / 4
         constexpr int COLS = Cfg::COLS;
+        if (epi == E_QKROPE) fill_rope_table(inv_tab, rp, 32 * EPI_WARPS);
         const int q = warp & 3;
         const int h = (warp - 2) >> 2;
         uint8_t *bufs = epi_buf + (warp - 2) * 2 * kStageBufBytes;
@@ -695,7 +717,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
             const int row = m0 + q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN + h * COLS;
             drain_accumulator<COLS, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
-                                              lane, rp);
+                                              lane, rp, inv_tab);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(leader_acc_empty[acc]);
