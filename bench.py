@@ -401,6 +401,7 @@ def ours(args):
             "roofline": {"bound": "tensor", "kernel": "linear_tcgen05 (all QKV/out/FFN projections)",
                          "achieved": gemm_tflops, "peak": sustained_tf, "unit": "TFLOP/s",
                          "frac": gemm_tflops / sustained_tf, "peak_kind": f"bf16 sustained, {peak_kind}",
+                         "frac_of_burst": gemm_tflops / burst_tf,
                          "traffic": traffic,
                          "traffic_note": "DRAM bytes per launch, mean of the four projection GEMMs of one layer "
                                          "(ncu, profiles/linear_tcgen05_pair_bge-large.md)",
