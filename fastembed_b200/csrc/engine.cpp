@@ -26,6 +26,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "fe_internal.h"
 #include "json_min.h"
 
@@ -204,13 +206,17 @@ fe_status ensure_activations(fe_engine *e, int64_t T)
     return FE_OK;
 }
 
+// One launch of the forward: counted, optionally timed with CUDA events on its stream,
+// and marked as an NVTX range (host side, for nsys and other NVTX tools; the range
+// brackets the launch call, not the kernel's execution) named after the op.
 struct Scope {
     fe_engine *e;
     int cat;
     cudaStream_t s;
     size_t idx = 0;
-    Scope(fe_engine *e_, int cat_, cudaStream_t s_) : e(e_), cat(cat_), s(s_)
+    Scope(fe_engine *e_, int cat_, cudaStream_t s_, const char *name = nullptr) : e(e_), cat(cat_), s(s_)
     {
+        nvtxRangePushA(name ? name : cat == CAT_GEMM ? "fe.linear" : cat == CAT_ATTN ? "fe.attention" : "fe.rows");
         e->stats.launches++;
         if (cat == CAT_GEMM) e->stats.gemm_launches++;
         if (!e->profiling) return;
@@ -230,6 +236,7 @@ struct Scope {
     ~Scope()
     {
         if (e->profiling) cudaEventRecord(e->ev[idx + 1], s);
+        nvtxRangePop();
     }
 };
 
@@ -255,7 +262,7 @@ fe_status linear(fe_engine *e, cudaStream_t s, const void *x, const DevBuf &w, c
 fe_status linear_ln(fe_engine *e, cudaStream_t s, const void *x, const DevBuf &w, const DevBuf &b, const DevBuf &g,
                     const DevBuf &beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k)
 {
-    Scope sc(e, CAT_GEMM, s);
+    Scope sc(e, CAT_GEMM, s, "fe.linear_layernorm");
     fe_status st = FE_OK;
     cudaError_t err = fe::launch_linear_layernorm(x, w.p, b.as<float>(), g.as<float>(), beta.as<float>(), h32, h16, m,
                                                   n, k, e->cfg.layer_norm_eps, e->ln_ws.p, e->y32.as<float>(), s, &st);
@@ -298,7 +305,7 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
     float *h32 = e->h32.as<float>();
     void *h16 = e->h16.p, *qkv = e->qkv.p, *attn = e->attn.p, *ff = e->ff.p;
     {
-        Scope sc(e, CAT_OTHER, s);
+        Scope sc(e, CAT_OTHER, s, "fe.embed_layernorm");
         FE_TRY_CUDA(fe::launch_embed_layernorm(ids, cu, batch, T, e->word.as<float>(), e->pos.as<float>(),
                                                e->type.as<float>(), e->emb_g.as<float>(), e->emb_b.as<float>(),
                                                static_cast<int>(D), c.vocab_size, c.max_position, c.layer_norm_eps,
@@ -310,7 +317,7 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
         const bool last = l + 1 == c.layers;
         FE_TRY(linear(e, s, h16, L.wqkv, L.bqkv, nullptr, qkv, T, 3 * D, D, FE_EPI_BIAS, FE_DTYPE_BF16));
         {
-            Scope sc(e, CAT_ATTN, s);
+            Scope sc(e, CAT_ATTN, s, "fe.attention");
             fe_status st = FE_OK;
             cudaError_t err = fe::launch_attention_varlen(qkv, cu, batch, max_len, c.heads,
                                                           static_cast<int>(D / c.heads), attn, T, false, s, &st);
@@ -321,7 +328,7 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
         // residual stream
         FE_TRY(linear(e, s, attn, L.wo, L.bo, nullptr, e->y32.p, T, D, D, FE_EPI_BIAS, FE_DTYPE_BF16));
         {
-            Scope sc(e, CAT_GEMM, s);
+            Scope sc(e, CAT_GEMM, s, "fe.residual_layernorm");
             FE_TRY_CUDA(fe::launch_layernorm_dual_bf16in(e->y32.p, h32, L.ln1_g.as<float>(), L.ln1_b.as<float>(), h32,
                                                          h16, T, static_cast<int>(D), c.layer_norm_eps, s));
         }
@@ -329,7 +336,7 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
         FE_TRY(linear_ln(e, s, ff, L.w2, L.b2, L.ln2_g, L.ln2_b, h32, last ? nullptr : h16, T, D, F));
     }
     {
-        Scope sc(e, CAT_OTHER, s);
+        Scope sc(e, CAT_OTHER, s, "fe.pool_l2");
         FE_TRY_CUDA(fe::launch_pool_l2(h32, cu, batch, static_cast<int>(D), c.pooling, out, s));
     }
     return FE_OK;
@@ -478,7 +485,7 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
     // pre-norm projection + residual + RMSNorm: fused where the launcher can (long K), else two launches
     auto linear_rms = [&](const void *x, const DevBuf &w, const DevBuf &norm_w, float *h, void *out16, int64_t n,
                           int64_t k) -> fe_status {
-        Scope sc(e, CAT_GEMM, s);
+        Scope sc(e, CAT_GEMM, s, "fe.linear_rmsnorm");
         fe_status st = FE_OK;
         cudaError_t err = fe::launch_linear_layernorm(x, w.p, e->zero_bias.as<float>(), norm_w.as<float>(), nullptr, h,
                                                       out16, T, n, k, eps, e->ln_ws.p, nullptr, s, &st, true);
@@ -486,14 +493,14 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
         return fe::check_cuda(err, "linear+RMSNorm");
     };
     {
-        Scope sc(e, CAT_OTHER, s);
+        Scope sc(e, CAT_OTHER, s, "fe.embed_scale");
         // Gemma3 scales the embeddings by sqrt(hidden) (rounded to fp32); Qwen3 does not
         const float escale = gemma ? static_cast<float>(std::sqrt(static_cast<double>(D))) : 1.0f;
         FE_TRY_CUDA(fe::launch_embed_scale(ids, T, e->word.as<float>(), c.vocab_size, static_cast<int>(D), escale, h32, s));
         FE_TRY_CUDA(fe::launch_token_positions(cu, batch, e->tpos.as<int32_t>(), s));
     }
     {
-        Scope sc(e, CAT_OTHER, s);
+        Scope sc(e, CAT_OTHER, s, "fe.rms_norm");
         FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, e->rlayers[0].in_norm.as<float>(), gemma, eps, T, static_cast<int>(D),
                                              nullptr, x16, s));
     }
@@ -507,7 +514,7 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
         const bool last = l + 1 == c.layers;
         if (fuse_rope) {
             // QKV projection with the q/k norms and RoPE in its epilogue
-            Scope sc(e, CAT_GEMM, s);
+            Scope sc(e, CAT_GEMM, s, "fe.qkv_qk_norm_rope");
             fe_status st = FE_OK;
             cudaError_t err = fe::launch_linear_qk_norm_rope(x16, L.wqkv.p, qkv, T, D, c.q_heads, c.kv_heads,
                                                              static_cast<int>(hd), L.q_norm.as<float>(),
@@ -517,13 +524,13 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
             FE_TRY_CUDA(err);
         } else {
             FE_TRY(gemm(x16, L.wqkv, nullptr, nullptr, qkv, QKV, D, FE_EPI_NONE, FE_DTYPE_BF16));
-            Scope sc(e, CAT_OTHER, s);
+            Scope sc(e, CAT_OTHER, s, "fe.qk_norm_rope");
             FE_TRY_CUDA(fe::launch_qk_norm_rope(qkv, cu, batch, T, c.q_heads, c.kv_heads, static_cast<int>(hd),
                                                 L.q_norm.as<float>(), L.k_norm.as<float>(), gemma, eps,
                                                 layer_theta(c, l), s, e->tpos.as<int32_t>()));
         }
         {
-            Scope sc(e, CAT_ATTN, s);
+            Scope sc(e, CAT_ATTN, s, "fe.attention_gqa");
             fe_status st = FE_OK;
             cudaError_t err = fe::launch_attention_wide(qkv, cu, batch, max_len, c.q_heads, c.kv_heads,
                                                         static_cast<int>(hd), !gemma, qscale, attn, T, s, &st);
@@ -539,7 +546,7 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
             FE_TRY(linear_rms(ff, L.wd, last ? e->final_norm : e->rlayers[l + 1].in_norm, h32, last ? nullptr : x16, D,
                               F));
             if (last) {
-                Scope sc(e, CAT_OTHER, s);
+                Scope sc(e, CAT_OTHER, s, "fe.rms_norm");
                 FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, next_norm, false, eps, T, static_cast<int>(D), fin, nullptr,
                                                      s));
             }
@@ -551,14 +558,14 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
             void *y16 = y32;
             FE_TRY(gemm(attn, L.wo, nullptr, nullptr, y16, D, AO, FE_EPI_NONE, FE_DTYPE_BF16));
             {
-                Scope sc(e, CAT_OTHER, s);
+                Scope sc(e, CAT_OTHER, s, "fe.rms_sandwich");
                 FE_TRY_CUDA(fe::launch_rms_sandwich(y16, L.post_attn_norm.as<float>(), h32, L.pre_ff_norm.as<float>(),
                                                     true, eps, T, static_cast<int>(D), nullptr, x16, s, true));
             }
             FE_TRY(gemm(x16, L.wgu, nullptr, nullptr, ff, 2 * F, D, FE_EPI_GEGLU, FE_DTYPE_BF16));
             FE_TRY(gemm(ff, L.wd, nullptr, nullptr, y16, D, F, FE_EPI_NONE, FE_DTYPE_BF16));
             {
-                Scope sc(e, CAT_OTHER, s);
+                Scope sc(e, CAT_OTHER, s, "fe.rms_sandwich");
                 FE_TRY_CUDA(fe::launch_rms_sandwich(y16, L.post_ff_norm.as<float>(), h32, next_norm, true, eps, T,
                                                     static_cast<int>(D), last ? fin : nullptr, last ? nullptr : x16,
                                                     s, true));
@@ -566,7 +573,7 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
         }
     }
     {
-        Scope sc(e, CAT_OTHER, s);
+        Scope sc(e, CAT_OTHER, s, "fe.pool_l2");
         FE_TRY_CUDA(fe::launch_pool_l2(fin, cu, batch, static_cast<int>(D), c.pooling, out, s));
     }
     return FE_OK;
