@@ -4,9 +4,10 @@
 One step = one forward pass (embed+LN, 24 post-LN layers, CLS pooling + L2) over
 the rank's slice of a batch of 256 sentences with lognormal lengths (median 96,
 sigma 0.6, truncated to [8, 512]), packed without padding.  With N GPUs
-(torchrun, one process per GPU) the global batch is 256*N sentences, sorted by
-length and cut into N contiguous slices of equal algorithmic FLOPs: replica data
-parallelism with no collective on the data path (weak scaling).
+(torchrun, one process per GPU) the global batch is 256*N sentences (the 256 lengths
+N times, fresh ids), sorted by length and cut into N contiguous slices of equal
+estimated time (fe_plan_shards: projection FLOPs plus a per-tile attention cost):
+replica data parallelism with no collective on the data path (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload bge-large|bge-small|bge-base|qwen3-0.6b|gemma-300m]
@@ -76,11 +77,14 @@ def peaks():
 
 # ------------------------------------------------------------------ workload
 def global_batch(shape, world, per_gpu=None):
+    """The batch of `world` GPUs: the per-GPU length sample taken `world` times (so every N
+    runs the same length mix and the same work per GPU), with fresh token ids throughout;
+    sorted by length, longest first."""
     if hasattr(shape, "family"):
-        lengths = W.sample_rms_lengths(shape, batch=(per_gpu or shape.batch) * world, seed=1)
+        lengths = np.tile(W.sample_rms_lengths(shape, batch=per_gpu or shape.batch, seed=1), world)
         ids = W.sample_rms_ids(shape, lengths, seed=1)
     else:
-        lengths = W.sample_lengths(shape, batch=(per_gpu or shape.batch) * world, seed=1)
+        lengths = np.tile(W.sample_lengths(shape, batch=per_gpu or shape.batch, seed=1), world)
         ids, _ = W.sample_ids(shape, lengths, seed=1, pad_to=int(lengths.max()))
     order = np.argsort(-lengths, kind="stable")
     return lengths[order], ids[order]
@@ -395,7 +399,8 @@ def ours(args):
             "config": {"workload": DESCRIPTIONS[args.workload],
                        "global_batch": int(sentences), "valid_tokens_per_step": int(tokens),
                        "tokens_per_s": tokens / (ms_per_step / 1e3),
-                       "parallelism": f"replica dp{world}, FLOP-balanced contiguous slices, no collective",
+                       "parallelism": f"replica dp{world}, cost-balanced contiguous slices of the length-sorted batch, "
+                                      "no collective",
                        "l2": "inputs larger than L2: the bf16 weights and the activations of a step are each "
                              "several times the 126 MB L2"},
             "roofline": {"bound": "tensor", "kernel": "linear_tcgen05 (all QKV/out/FFN projections)",

@@ -6,8 +6,8 @@
 // in front and [SEP]=102 behind, :11-27) and run every sentence of the batch in one
 // packed device pass per GPU instead of a per-text loop (:359-365).  With FE_DEVICES
 // listing several GPUs, a batch is sorted by length and cut into contiguous slices of
-// equal algorithmic work, one per GPU, each run by its own host thread; there is no
-// device-to-device traffic.
+// equal estimated time (fe_plan_shards: projection FLOPs plus a per-tile attention cost),
+// one per GPU, each run by its own host thread; there is no device-to-device traffic.
 #include <cuda_runtime.h>
 
 #include <algorithm>

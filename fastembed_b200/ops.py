@@ -346,15 +346,16 @@ def pack(ids: np.ndarray, lengths: np.ndarray):
 
 
 def plan_shards(shape, sorted_lengths: np.ndarray, parts: int) -> list[int]:
-    """Contiguous FLOP-balanced cut points of a length-sorted batch (fe_plan_shards for the
-    BERT family; fe_plan_shards_costs over the shape's own per-sentence FLOPs for the
-    Qwen3 / Gemma3 shapes)."""
+    """Contiguous cost-balanced cut points of a length-sorted batch (fe_plan_shards for the
+    BERT family, whose cost adds a per-tile attention term to the projection FLOPs;
+    fe_plan_shards_costs over the shape's own per-sentence FLOPs for the Qwen3 / Gemma3
+    shapes)."""
     L = np.ascontiguousarray(sorted_lengths, dtype=np.int32)
     cuts = np.zeros(max(parts - 1, 1), np.int32)
     if hasattr(shape, "family"):
         if L.size > 1 and np.any(L[1:] > L[:-1]):
             raise ValueError("plan_shards: lengths must be sorted in descending order")
-        costs = np.array([shape.flops_per_sentence(int(x)) for x in L], np.float64)
+        costs = np.array([shape.shard_cost(int(x)) for x in L], np.float64)
         call("fe_plan_shards_costs", costs.ctypes.data_as(C.c_void_p), L.size, parts,
              cuts.ctypes.data_as(C.c_void_p))
     else:

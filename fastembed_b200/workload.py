@@ -57,6 +57,14 @@ class EncoderShape:
     def attn_flops_per_sentence(self, length: int) -> float:
         return self.layers * 4.0 * length * length * self.hidden
 
+    def shard_cost(self, length: int) -> float:
+        """The cost fe_plan_shards balances, in projection FLOPs: the GEMM FLOPs plus, per
+        head and layer, three times the full-tile FLOPs (4 x 128 x 128 x head_dim) for each
+        (128-query, 128-key) attention tile the sentence occupies (the attention kernel's time
+        goes by tiles, and a tile takes about that long at the projections' rate)."""
+        tiles = -(-int(length) // 128)
+        return self.gemm_flops_per_sentence(length) + self.layers * self.heads * tiles * tiles * 3.0 * 4.0 * 128 * 128 * self.head_dim
+
 
 SHAPES = {
     # BGE-small-zh shape: 4 layers, D 512, 8 heads, FFN 2048; batch 8, L ~ U[16,128]
@@ -182,11 +190,11 @@ def config_json(shape: EncoderShape) -> dict:
 
 
 def balanced_cuts(shape: EncoderShape, sorted_lengths: np.ndarray, parts: int) -> list[int]:
-    """Contiguous cut points of a length-sorted batch into `parts` slices whose
-    algorithmic FLOPs are as equal as a greedy prefix cut gets them."""
+    """Contiguous cut points of a length-sorted batch into `parts` slices whose costs
+    (EncoderShape.shard_cost) are as equal as a greedy prefix cut gets them."""
     if parts <= 1:
         return []
-    w = np.array([shape.flops_per_sentence(int(L)) for L in sorted_lengths], dtype=np.float64)
+    w = np.array([shape.shard_cost(int(L)) for L in sorted_lengths], dtype=np.float64)
     prefix = np.concatenate([[0.0], np.cumsum(w)])  # prefix[i] = work of the first i sentences
     total = prefix[-1]
     cuts: list[int] = []
@@ -245,6 +253,11 @@ class RmsShape:
 
     def flops_per_sentence(self, length: int) -> float:
         return self.gemm_flops_per_sentence(length) + self.attn_flops_per_sentence(length)
+
+    def shard_cost(self, length: int) -> float:
+        """The cost the shard planner balances (fe_plan_shards_costs): the algorithmic FLOPs;
+        these sentences fill most of their attention tiles."""
+        return self.flops_per_sentence(length)
 
 
 RMS_SHAPES = {

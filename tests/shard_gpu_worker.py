@@ -2,7 +2,7 @@
 torch.distributed.run, not collected by pytest).
 
 Every rank builds the same bge-base-shaped batch, sorts it by length, takes its
-FLOP-balanced contiguous slice (fe_plan_shards), encodes the slice with its own engine on
+cost-balanced contiguous slice (fe_plan_shards), encodes the slice with its own engine on
 GPU rank % device_count, and the slices are gathered over gloo to rank 0, which writes
 the embeddings in the sorted order to the output file.  With fewer GPUs than ranks, the
 ranks that share a GPU run every projection + norm step as two launches

@@ -1,6 +1,6 @@
 """The C ABI without a GPU: the library loads, exports every function that
 include/fastembed_b200.h declares, validates arguments before touching the device,
-and its host-only helpers (batch packing, FLOP-balanced shard planning) are right."""
+and its host-only helpers (batch packing, cost-balanced shard planning) are right."""
 import ctypes as C
 import os
 import re
@@ -111,7 +111,7 @@ def test_plan_shards_matches_python_and_balances(fe_lib, parts):
     assert cuts == W.balanced_cuts(shape, L, parts)
     assert cuts == sorted(cuts) and 0 < cuts[0] and cuts[-1] < L.size
     bounds = [0] + cuts + [L.size]
-    work = [sum(shape.flops_per_sentence(int(x)) for x in L[a:b]) for a, b in zip(bounds, bounds[1:])]
+    work = [sum(shape.shard_cost(int(x)) for x in L[a:b]) for a, b in zip(bounds, bounds[1:])]
     assert max(work) / (sum(work) / parts) < 1.02  # within 2% of a perfect split
     with pytest.raises(Exception):
         ops.plan_shards(shape, L[::-1].copy(), parts)  # ascending order is rejected
@@ -138,7 +138,7 @@ def test_plan_shards_costs_matches_the_bert_planner(fe_lib):
     from fastembed_b200 import capi, ops, workload as W
     shape = W.SHAPES["bge-base"]
     L = np.sort(W.sample_lengths(shape, batch=500, seed=3))[::-1].copy()
-    costs = np.array([shape.flops_per_sentence(int(x)) for x in L], np.float64)
+    costs = np.array([shape.shard_cost(int(x)) for x in L], np.float64)
     for parts in (1, 3, 8):
         cuts = np.zeros(max(parts - 1, 1), np.int32)
         capi.call("fe_plan_shards_costs", costs.ctypes.data_as(C.c_void_p), L.size, parts,

@@ -8,7 +8,7 @@
   (F32 or BF16 entries) must tokenize exactly as the reference's WordPiece does and embed
   within the stated tolerance of the oracle forward; encode() of one text must equal its
   row of encode_batch() bit for bit; FE_DEVICES="0,0" (two engines, two host threads,
-  FLOP-balanced slices) must give the same bits as one engine.
+  cost-balanced slices) must give the same bits as one engine.
 """
 import dataclasses
 import os

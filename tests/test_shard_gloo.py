@@ -1,5 +1,5 @@
 """The multi-GPU data path on CPU: world_size-2 gloo ranks each take their
-FLOP-balanced contiguous slice of a length-sorted batch (fe_plan_shards) and encode
+cost-balanced contiguous slice of a length-sorted batch (fe_plan_shards) and encode
 it (here with the oracle standing in for the GPU engine); the gathered embeddings,
 scattered back to the original order, must equal a single-process run bit for bit.
 A rank that fails is seen by the others on the host, before any further work."""

@@ -1,6 +1,6 @@
 """The sharded data path with the GPU engine in every rank: two torch.distributed.run
 processes (one per GPU, or both on GPU 0 when only one is visible) each encode their
-FLOP-balanced contiguous slice of a length-sorted 64-sentence bge-base-shaped batch, and
+cost-balanced contiguous slice of a length-sorted 64-sentence bge-base-shaped batch, and
 the gathered slices must equal one engine's encode of the whole batch bit for bit (each
 sentence's embedding does not depend on the rest of its batch).  The gloo test
 (tests/test_shard_gloo.py) covers the same path on the CPU with the oracle in place of
