@@ -324,10 +324,13 @@ fe_status forward(fe_engine *e, const int32_t *ids, const int32_t *cu, const int
             if (st != FE_OK) return st;
             FE_TRY_CUDA(err);
         }
-        // out-proj + bias (bf16, into the y32 buffer) then residual + LayerNorm, in place on the fp32
-        // residual stream
-        FE_TRY(linear(e, s, attn, L.wo, L.bo, nullptr, e->y32.p, T, D, D, FE_EPI_BIAS, FE_DTYPE_BF16));
-        {
+        if (fe::ln_cluster_applies(D, D, false, false)) {
+            // out-proj + bias + residual + LayerNorm in one launch: one cluster per 128-row block
+            FE_TRY(linear_ln(e, s, attn, L.wo, L.bo, L.ln1_g, L.ln1_b, h32, h16, T, D, D));
+        } else {
+            // out-proj + bias (bf16, into the y32 buffer) then residual + LayerNorm, in place on the fp32
+            // residual stream
+            FE_TRY(linear(e, s, attn, L.wo, L.bo, nullptr, e->y32.p, T, D, D, FE_EPI_BIAS, FE_DTYPE_BF16));
             Scope sc(e, CAT_GEMM, s, "fe.residual_layernorm");
             FE_TRY_CUDA(fe::launch_layernorm_dual_bf16in(e->y32.p, h32, L.ln1_g.as<float>(), L.ln1_b.as<float>(), h32,
                                                          h16, T, static_cast<int>(D), c.layer_norm_eps, s));

@@ -73,6 +73,10 @@ fe_status make_tmap_heads(CUtensorMap *map, const void *base, uint64_t heads, ui
 cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
                                const float *residual, void *y, int64_t m, int64_t n, int64_t k,
                                int epilogue, int y_dtype, cudaStream_t s, fe_status *st);
+// True when launch_linear_layernorm runs the step as linear_ln_cluster (LayerNorm, n a
+// multiple of 256 from 512 to 1024, k a multiple of 64; by default only where the pair kernel
+// would not fuse: pair_fused is that decision).
+bool ln_cluster_applies(int64_t n, int64_t k, bool rms, bool pair_fused);
 // QKV projection y = x W^T [m, (q_heads + 2 kv_heads) * head_dim] in bf16, no bias, with the
 // per-head RMSNorm (w, or 1 + w when one_plus) and rotate-half RoPE (positions pos[m], base
 // theta) of the query and key heads applied in the GEMM epilogue; value heads as they are.

@@ -1425,6 +1425,537 @@ LnVariant pick_ln_variant(int64_t k)
 }
 }  // namespace
 
+namespace {
+// ---------------------------------------------------------------------------
+// Linear + residual + LayerNorm for rows of up to 1024 columns, one cluster per row block:
+//     h32 <- LayerNorm((x W^T + bias) + h32) * gamma + beta,   h16 <- bf16(h32)
+// the out-projection step of a post-LN encoder layer (reference:
+// src/sentence_transformers_impl.cpp:250-266).  A cluster of R = N / 256 CTAs (one per SM)
+// owns a 128-row block; CTA r computes columns [256 r, 256 r + 256) with 1-CTA tcgen05
+// MMAs into one of two 256-column TMEM accumulators, so one row block's epilogue overlaps
+// the next one's mainloop.  Each epilogue thread owns a row: it forms x = acc + bias +
+// residual in TMEM with per-32-column exact two-pass statistics, sends its (mean, M2)
+// over 256 columns to every CTA of the cluster through distributed shared memory
+// (st.shared::cluster + a remote mbarrier arrive, release / acquire at cluster scope),
+// combines the R parts in rank order (so every CTA and every run gets the same bits),
+// then normalises from TMEM and TMA-stores fp32 and bf16.  Unlike the pair kernel's
+// global-memory exchange, the statistics never leave the GPC, and the cluster is
+// co-scheduled by the hardware, so no grid-residency assumption is made.
+constexpr int LC_STAGES = 3;
+constexpr int LC_BN = 256;
+constexpr int LC_MAX_R = 4;                       // rows of up to 1024 columns
+constexpr uint32_t LC_STAGE = BM * BK * 2 + LC_BN * BK * 2;  // x tile + W tile, 48 KB
+constexpr uint32_t LC_FSLAB = 32 * 32 * 4;        // one warp's fp32 32 x 32 slab: residual in, output out
+constexpr uint32_t LC_BSLAB = 32 * 32 * 2;        // its bf16 32 x 32 output slab
+constexpr int LC_RSLABS = 3;                      // fp32 slabs per warp (residual chunks in flight)
+constexpr uint32_t LC_WARP = LC_RSLABS * LC_FSLAB + 2 * LC_BSLAB;
+constexpr uint32_t LC_EPI = kEpiWarps * LC_WARP;
+constexpr uint32_t LC_STATS = 2 * LC_MAX_R * BM * 8;                 // [tile parity][rank][row] (mean, M2)
+constexpr uint32_t LC_VEC = 3 * LC_BN * 4;                           // bias, gamma, beta of this CTA's columns
+constexpr uint32_t LC_BAR = 256;
+constexpr uint32_t LC_SMEM = 1024 + LC_STAGES * LC_STAGE + LC_EPI + LC_STATS + LC_VEC + LC_BAR;
+static_assert(LC_SMEM <= 227 * 1024, "shared memory budget");
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire: the peers' distributed-shared-memory writes
+// made before their release arrives are visible after it.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity)
+{
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t limit = wait_limit_ns();
+    const bool every = limit < kShortWaitNs;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (((i & 255u) == 0 || every) && globaltimer_ns() - t0 > limit) return false;
+    }
+}
+
+// Asynchronous store of (a, b) into the shared memory of a CTA of the cluster (shared::cluster
+// address `addr`); its 8 bytes count as completed transaction bytes on that CTA's mbarrier at
+// `bar` (shared::cluster address), so the receiver's phase completes once every expected byte
+// has landed, with no fence on the sending side.
+__device__ __forceinline__ void st_async_v2(uint32_t addr, float a, float b, uint32_t bar)
+{
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+                 "f"(a), "f"(b), "r"(bar)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_ln_cluster(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                      const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_h16, int M,
+                      int N, int K, const float *__restrict__ bias, const float *__restrict__ gamma,
+                      const float *__restrict__ beta, float *h32, float eps, int write16, int *status)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = smem;
+    uint8_t *epi_buf = ring + LC_STAGES * LC_STAGE;      // per warp: 2 x (fp32 slab, bf16 slab)
+    float2 *stats = reinterpret_cast<float2 *>(epi_buf + LC_EPI);  // [2][LC_MAX_R][BM]
+    float *vb = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(stats) + LC_STATS);
+    float *vg = vb + LC_BN, *ve = vg + LC_BN;
+    uint64_t *full = reinterpret_cast<uint64_t *>(ve + LC_BN);
+    uint64_t *empty = full + LC_STAGES;
+    uint64_t *acc_full = empty + LC_STAGES;  // [2]
+    uint64_t *acc_empty = acc_full + 2;      // [2]
+    uint64_t *stat_bar = acc_empty + 2;      // [2] by row-block parity: the cluster's statistics landed
+    uint64_t *rbar_all = stat_bar + 2;       // [kEpiWarps][LC_RSLABS] residual slab landed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rbar_all + kEpiWarps * LC_RSLABS);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int R = N / LC_BN;                         // CTAs per cluster (the cluster dimension)
+    const uint32_t rank = cluster_ctarank();
+    const int cluster = static_cast<int>(blockIdx.x) / R;
+    const int nclusters = static_cast<int>(gridDim.x) / R;
+    const int m_tiles = (M + BM - 1) / BM;
+    const int k_iters = (K + BK - 1) / BK;
+    const int n0 = static_cast<int>(rank) * LC_BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < LC_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 32 * kEpiWarps);
+            mbar_init(&stat_bar[b], 1);  // armed by this CTA with the bytes the cluster sends it
+        }
+        for (int i = 0; i < kEpiWarps * LC_RSLABS; ++i) mbar_init(&rbar_all[i], 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_h);
+        tma_prefetch_desc(&tm_h16);
+    }
+    grid_dep_wait();
+    for (int i = threadIdx.x; i < LC_BN; i += blockDim.x) {
+        vb[i] = bias[n0 + i];
+        vg[i] = gamma[n0 + i];
+        ve[i] = beta[n0 + i];
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 2 * LC_BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // every CTA's barriers exist before any remote arrive
+    tc_fence_after();
+    grid_dep_launch();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer: x rows of the row block, W rows n0 .. n0 + 255
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, armed_parity = 0;
+            for (int t = cluster; t < m_tiles && !*abort_flag; t += nclusters) {
+                const int m0 = t * BM;
+                for (int kb = 0; kb < k_iters; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1)) {
+                        report(status, DEV_TIMEOUT);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t *a_dst = ring + stage * LC_STAGE;
+                    uint8_t *b_dst = a_dst + BM * BK * 2;
+                    mbar_arrive_expect_tx(&full[stage], LC_STAGE);
+                    tma_load_2d(a_dst, &tm_x, &full[stage], kb * BK, m0);
+                    tma_load_2d(b_dst, &tm_w, &full[stage], kb * BK, n0);
+                    armed |= 1u << stage;
+                    armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == LC_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            for (int s = 0; s < LC_STAGES; ++s)
+                if (armed & (1u << s))
+                    if (!mbar_wait_drain(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer: 128 x 256 per row block, accumulators alternate
+            constexpr uint32_t idesc = idesc_bf16_f32(BM, LC_BN, false, false);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool issued = false;
+            for (int t = cluster; t < m_tiles && !*abort_flag; t += nclusters) {
+                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) {
+                    report(status, DEV_TIMEOUT);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * LC_BN;
+                for (int kb = 0; kb < k_iters; ++kb) {
+                    if (!mbar_wait(&full[stage], phase)) {
+                        report(status, DEV_TIMEOUT);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(ring + stage * LC_STAGE);
+                    const uint32_t b_addr = a_addr + BM * BK * 2;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_f16_ss(d_tmem, sdesc_sw128(a_addr + k * 32, 16, 1024), sdesc_sw128(b_addr + k * 32, 16, 1024),
+                                    idesc, (kb | k) != 0 ? 1u : 0u);
+                    issued = true;
+                    umma_commit(&empty[stage]);
+                    if (++stage == LC_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (*abort_flag) break;
+                umma_commit(&acc_full[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+            if (*abort_flag && issued) {
+                uint64_t *probe = &acc_full[acc];
+                umma_commit(probe);
+                if (!mbar_wait_drain(probe, acc_phase)) report(status, DEV_TIMEOUT);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5): thread = row of the row block
+        const int q = warp & 3;  // TMEM lane quarter
+        const int wi = warp - 2;
+        uint8_t *wbuf = epi_buf + wi * LC_WARP;  // LC_RSLABS fp32 slabs, then 2 bf16 slabs
+        uint64_t *rbar = rbar_all + wi * LC_RSLABS;
+        uint32_t rpar = 0, inflight = 0;          // per slab: parity to wait for / a load in flight
+        const float inv_n = 1.0f / static_cast<float>(N);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        uint32_t it = 0;  // row blocks done by this CTA
+        // residual chunk c (32 rows x 32 columns of h32) into slab `sl`, by TMA
+        auto load_res = [&](int sl, int c, int row0) {
+            mbar_arrive_expect_tx(&rbar[sl], LC_FSLAB);
+            tma_load_2d(wbuf + sl * LC_FSLAB, &tm_h, &rbar[sl], n0 + 32 * c, row0);
+        };
+        for (int t = cluster; t < m_tiles; t += nclusters, ++it) {
+            if (*abort_flag) break;
+            const int row0 = t * BM + q * 32;
+            const int p = static_cast<int>(it & 1);
+            constexpr int CH = LC_BN / 32;
+            // this row block's statistics: R parts x 128 rows x 8 bytes from the cluster (the
+            // barrier's previous phase of this parity, two row blocks ago, has completed)
+            if (threadIdx.x == 64) mbar_arrive_expect_tx(&stat_bar[p], static_cast<uint32_t>(R) * BM * 8);
+            // the previous row block's stores have read every slab; then the first residual chunks
+            if (lane == 0) {
+                bulk_wait_read<0>();
+                for (int c = 0; c < LC_RSLABS; ++c) load_res(c, c, row0);
+            }
+            inflight = (1u << LC_RSLABS) - 1;
+            __syncwarp();
+            if (!mbar_wait(&acc_full[acc], acc_phase)) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * LC_BN;
+
+            // ---- pass 1: x = (acc + bias) + residual back into TMEM; per-chunk mean and M2
+            float cm[CH], cq_sum = 0.f;
+            bool ok = true;
+            uint32_t vv[2][32];  // TMEM chunks: the next one loads while this one is worked on
+            tmem_ld_x32(t_row, vv[0]);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int sl = c % LC_RSLABS;
+                uint32_t(&v)[32] = vv[c & 1];
+                tmem_wait_ld_regs(v);
+                if (c + 1 < CH) {
+                    if (c >= 1) tmem_wait_st();  // vv[(c + 1) & 1] was the source of chunk c - 1's store
+                    tmem_ld_x32(t_row + (c + 1) * 32, vv[(c + 1) & 1]);
+                }
+                if (!mbar_wait(&rbar[sl], (rpar >> sl) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                rpar ^= 1u << sl;
+                inflight &= ~(1u << sl);
+                const uint8_t *rs = wbuf + sl * LC_FSLAB + lane * 128;
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 r = *reinterpret_cast<const uint4 *>(rs + ((j ^ (lane & 7)) << 4));
+                    const float4 bb = *reinterpret_cast<const float4 *>(vb + c * 32 + 4 * j);
+                    float x0 = __uint_as_float(v[4 * j + 0]), x1 = __uint_as_float(v[4 * j + 1]);
+                    float x2 = __uint_as_float(v[4 * j + 2]), x3 = __uint_as_float(v[4 * j + 3]);
+                    add_f32x2(x0, x1, bb.x, bb.y);
+                    add_f32x2(x2, x3, bb.z, bb.w);
+                    add_f32x2(x0, x1, __uint_as_float(r.x), __uint_as_float(r.y));
+                    add_f32x2(x2, x3, __uint_as_float(r.z), __uint_as_float(r.w));
+                    add_f32x2(s4[0], s4[1], x0, x1);
+                    add_f32x2(s4[2], s4[3], x2, x3);
+                    v[4 * j + 0] = __float_as_uint(x0);
+                    v[4 * j + 1] = __float_as_uint(x1);
+                    v[4 * j + 2] = __float_as_uint(x2);
+                    v[4 * j + 3] = __float_as_uint(x3);
+                }
+                __syncwarp();  // every lane has read the slab: it takes chunk c + LC_RSLABS
+                if (c + LC_RSLABS < CH) {
+                    if (lane == 0) load_res(sl, c + LC_RSLABS, row0);
+                    inflight |= 1u << sl;
+                }
+                cm[c] = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 32.0f);
+                float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    float d0 = __uint_as_float(v[j]), d1 = __uint_as_float(v[j + 1]);
+                    add_f32x2(d0, d1, -cm[c], -cm[c]);
+                    fma_f32x2v(q4[j & 3], q4[(j & 3) + 1], d0, d1, d0, d1, q4[j & 3], q4[(j & 3) + 1]);
+                }
+                cq_sum += (q4[0] + q4[1]) + (q4[2] + q4[3]);
+                tmem_st_x32(t_row + c * 32, v);
+            }
+            tmem_wait_ld();
+            tmem_wait_st();
+            if (!ok) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            // (mean, M2) of this row over the CTA's 256 columns: equal-size chunks combined exactly
+            float mean = 0.f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) mean += cm[c];
+            mean *= 1.0f / CH;
+            float m2 = 0.f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const float d = cm[c] - mean;
+                m2 += d * d;
+            }
+            m2 = cq_sum + 32.0f * m2;
+
+            // ---- exchange: this part to every CTA of the cluster, then the row's R parts
+            float2 *slot = stats + (p * LC_MAX_R + static_cast<int>(rank)) * BM + q * 32 + lane;
+            for (int k = 0; k < R; ++k)
+                st_async_v2(map_to_rank(slot, static_cast<uint32_t>(k)), mean, m2,
+                            map_to_rank(&stat_bar[p], static_cast<uint32_t>(k)));
+            if (!mbar_wait_cluster(&stat_bar[p], (it >> 1) & 1)) {
+                report(status, DEV_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+            float gm = 0.f;
+            float2 part[LC_MAX_R];
+#pragma unroll
+            for (int k = 0; k < LC_MAX_R; ++k)
+                if (k < R) {
+                    part[k] = stats[(p * LC_MAX_R + k) * BM + q * 32 + lane];
+                    gm += part[k].x;
+                }
+            gm /= static_cast<float>(R);
+            float gq = 0.f, gd = 0.f;
+#pragma unroll
+            for (int k = 0; k < LC_MAX_R; ++k)
+                if (k < R) {
+                    const float d = part[k].x - gm;
+                    gq += part[k].y;
+                    gd += d * d;
+                }
+            gq += static_cast<float>(LC_BN) * gd;
+            const float inv_sd = 1.0f / sqrtf(gq * inv_n + eps);
+
+            // ---- pass 2: normalise from TMEM; per 32-column chunk an fp32 slab (128B swizzle)
+            // and a bf16 slab (64B swizzle), TMA-stored as one bulk group, double-buffered
+            tmem_ld_x32(t_row, vv[0]);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                uint32_t(&v)[32] = vv[c & 1];
+                tmem_wait_ld_regs(v);
+                if (c + 1 < CH) tmem_ld_x32(t_row + (c + 1) * 32, vv[(c + 1) & 1]);
+                float o[32];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 g = *reinterpret_cast<const float4 *>(vg + c * 32 + 4 * j);
+                    const float4 e = *reinterpret_cast<const float4 *>(ve + c * 32 + 4 * j);
+                    float t0 = __uint_as_float(v[4 * j + 0]), t1 = __uint_as_float(v[4 * j + 1]);
+                    float t2 = __uint_as_float(v[4 * j + 2]), t3 = __uint_as_float(v[4 * j + 3]);
+                    add_f32x2(t0, t1, -gm, -gm);
+                    add_f32x2(t2, t3, -gm, -gm);
+                    mul_f32x2(t0, t1, inv_sd, inv_sd);
+                    mul_f32x2(t2, t3, inv_sd, inv_sd);
+                    fma_f32x2v(o[4 * j + 0], o[4 * j + 1], t0, t1, g.x, g.y, e.x, e.y);
+                    fma_f32x2v(o[4 * j + 2], o[4 * j + 3], t2, t3, g.z, g.w, e.z, e.w);
+                }
+                uint8_t *fs = wbuf + (c % LC_RSLABS) * LC_FSLAB;
+                uint8_t *bs = wbuf + LC_RSLABS * LC_FSLAB + (c & 1) * LC_BSLAB;
+                if (lane == 0) bulk_wait_read<1>();  // the groups of chunks up to c - 2 have read their slabs
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<uint4 *>(fs + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_uint4(__float_as_uint(o[4 * j + 0]), __float_as_uint(o[4 * j + 1]),
+                                   __float_as_uint(o[4 * j + 2]), __float_as_uint(o[4 * j + 3]));
+                if (write16) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        *reinterpret_cast<uint4 *>(bs + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                            make_uint4(pack_bf16x2(o[8 * j + 0], o[8 * j + 1]), pack_bf16x2(o[8 * j + 2], o[8 * j + 3]),
+                                       pack_bf16x2(o[8 * j + 4], o[8 * j + 5]), pack_bf16x2(o[8 * j + 6], o[8 * j + 7]));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tm_h, fs, n0 + c * 32, row0);
+                    if (write16) tma_store_2d(&tm_h16, bs, n0 + c * 32, row0);
+                    bulk_commit();
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+        // residual loads still in flight (an abandoned row block) land before the CTA exits
+        if (lane == 0) {
+            for (int sl = 0; sl < LC_RSLABS; ++sl)
+                if (inflight & (1u << sl))
+                    if (!mbar_wait_drain(&rbar[sl], (rpar >> sl) & 1u)) report(status, DEV_TIMEOUT);
+            bulk_wait_all<0>();
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while a peer may still write its shared memory or arrive on it
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 2 * LC_BN);
+    }
+}
+
+// FE_LN_CLUSTER: 0 = never use linear_ln_cluster; "all" = also where the pair kernel would
+// fuse (K >= 2048, for comparison); otherwise (default) for the shapes the pair kernel leaves
+// to two launches.
+int ln_cluster_mode()
+{
+    const char *v = getenv("FE_LN_CLUSTER");
+    if (v && v[0] == '0') return 0;
+    if (v && v[0] == 'a') return 2;
+    return 1;
+}
+
+// Clusters of linear_ln_cluster with R CTAs that can be resident at once (0 if unknown).
+int ln_cluster_resident(int R)
+{
+    static int cached[64][LC_MAX_R + 1] = {};
+    static uint64_t cached_ctx[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t ctx = current_context_id();
+    if (dev < 64 && cached_ctx[dev] == ctx && cached[dev][R] > 0) return cached[dev][R];
+    if (cudaFuncSetAttribute(linear_ln_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize, LC_SMEM) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = R;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(R, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = LC_SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, linear_ln_cluster, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (dev < 64) {
+        if (cached_ctx[dev] != ctx) {
+            for (int r = 0; r <= LC_MAX_R; ++r) cached[dev][r] = 0;
+            cached_ctx[dev] = ctx;
+        }
+        cached[dev][R] = clusters;
+    }
+    return clusters;
+}
+
+cudaError_t launch_ln_cluster(const void *x, const void *w, const float *bias, const float *gamma, const float *beta,
+                              float *h32, void *h16, int64_t m, int64_t n, int64_t k, float eps, cudaStream_t s,
+                              fe_status *st)
+{
+    const int R = static_cast<int>(n / LC_BN);
+    CUtensorMap tx, tw, th, th16;
+    fe_status r = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, k, k, BM, BK);
+    if (r == FE_OK) r = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, k, k, LC_BN, BK);
+    if (r == FE_OK) r = make_tmap_2d(&th, h32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, n, n, 32, 32);
+    if (r == FE_OK)
+        r = h16 ? make_tmap_2d(&th16, h16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, n, n, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_64B)
+                : make_tmap_2d(&th16, h32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, n, n, 32, 32);  // not used
+    if (r != FE_OK) {
+        *st = r;
+        return cudaSuccess;
+    }
+    const int resident = ln_cluster_resident(R);
+    if (resident < 1) {
+        *st = fail(FE_ERR_UNSUPPORTED, "linear+LayerNorm: no cluster of this size fits on the device");
+        return cudaSuccess;
+    }
+    const int m_tiles = static_cast<int>((m + BM - 1) / BM);
+    int nclusters = std::min(resident, current_sm_count() / R);
+    if (nclusters > m_tiles) nclusters = m_tiles;
+    if (nclusters < 1) nclusters = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = R;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(R * nclusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = LC_SMEM;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
+    return cudaLaunchKernelEx(&cfg, linear_ln_cluster, tx, tw, th, th16, M, N, K, bias, gamma, beta ? beta : gamma, h32,
+                              eps, h16 ? 1 : 0, current_device_status_word());
+}
+
+}  // namespace
+
+bool ln_cluster_applies(int64_t n, int64_t k, bool rms, bool pair_fused)
+{
+    const int mode = ln_cluster_mode();
+    if (rms || mode == 0 || n % LC_BN != 0 || n / LC_BN < 2 || n / LC_BN > LC_MAX_R || k % BK != 0) return false;
+    return mode == 2 || !pair_fused;
+}
+
 cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *bias, const float *gamma,
                                     const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
                                     float eps, void *stats, float *y_fallback, cudaStream_t s, fe_status *st, bool rms)
@@ -1443,6 +1974,7 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
         if (pairs > tiles) pairs = tiles;
         fused = pairs >= n_tiles;
     }
+    if (ln_cluster_applies(n, k, rms, fused)) return launch_ln_cluster(x, w, bias, gamma, beta, h32, h16, m, n, k, eps, s, st);
     if (!fused && rms) {
         // Unfused pre-norm form: x = x W^T + b + h32 in place, then RMSNorm into h16.
         cudaError_t e = launch_linear_bf16(x, w, bias, h32, h32, m, n, k, FE_EPI_BIAS_RESIDUAL, FE_DTYPE_F32, s, st);

@@ -313,6 +313,34 @@ def test_linear_layernorm(cuda_dev, monkeypatch, m, n, k, pair):
     ops.device_status(0)
 
 
+# (m, n, k, mode): the cluster form (linear_ln_cluster: R = n / 256 CTAs per 128-row block,
+# row statistics exchanged through distributed shared memory) at 2, 3 and 4 CTAs, one
+# row, partial and exact row blocks, the bge-large out-projection shape, and K = 4096
+# (FE_LN_CLUSTER=all takes it there too)
+LINEAR_LN_CLUSTER_SHAPES = [(1, 1024, 1024, "1"), (129, 512, 1024, "1"), (4097, 768, 768, "1"), (256, 1024, 1024, "1"),
+                            (26508, 1024, 1024, "1"), (700, 1024, 4096, "all"), (3001, 768, 3072, "all")]
+
+
+@pytest.mark.parametrize("m,n,k,mode", LINEAR_LN_CLUSTER_SHAPES)
+def test_linear_layernorm_cluster(cuda_dev, monkeypatch, m, n, k, mode):
+    """The cluster form against the fp32 composition of the same steps; repeated calls and a
+    row block computed alone are bit-identical to the batch (each row depends only on itself)."""
+    from fastembed_b200 import ops
+    monkeypatch.setenv("FE_LN_CLUSTER", mode)
+    x, w, b, res, gam, bet = _linear_ln_inputs(m, n, k, m + n + k + 1, cuda_dev)
+    ref = _linear_ln_ref(x, w, b, res, gam, bet, 1e-12)
+    h32, h16 = ops.linear_layernorm(x, w, b, gam, bet, res.clone(), 1e-12)
+    again, _ = ops.linear_layernorm(x, w, b, gam, bet, res.clone(), 1e-12)
+    torch.cuda.synchronize()
+    assert float((h32 - ref).abs().max()) < 1e-4
+    assert torch.equal(h16, h32.to(torch.bfloat16))
+    assert torch.equal(again, h32)
+    if m > 200:
+        part, _ = ops.linear_layernorm(x[37:200].contiguous(), w, b, gam, bet, res[37:200].clone(), 1e-12)
+        assert torch.equal(part, h32[37:200])
+    ops.device_status(0)
+
+
 def test_linear_layernorm_workspace_reuse_and_determinism(cuda_dev):
     """One workspace sized for the largest m serves calls with smaller m in between
     (every call leaves its counters at zero); repeated calls are bit-identical, a row
