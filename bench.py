@@ -385,7 +385,7 @@ def ours(args):
 
     if rank == 0:
         traffic = None
-        tpath = os.path.join(ROOT, "profiles", "linear_tcgen05_pair_bge-large.md")
+        tpath = os.path.join(ROOT, "profiles", "projections_bge-large.md")
         if os.path.exists(tpath) and args.workload == "bge-large":
             with open(tpath) as f:
                 for ln in f:
@@ -403,17 +403,19 @@ def ours(args):
                                       "no collective",
                        "l2": "inputs larger than L2: the bf16 weights and the activations of a step are each "
                              "several times the 126 MB L2"},
-            "roofline": {"bound": "tensor", "kernel": "linear_tcgen05 (all QKV/out/FFN projections)",
-                         "achieved": gemm_tflops, "peak": sustained_tf, "unit": "TFLOP/s",
-                         "frac": gemm_tflops / sustained_tf, "peak_kind": f"bf16 sustained, {peak_kind}",
-                         "frac_of_burst": gemm_tflops / burst_tf,
+            "roofline": {"bound": "tensor",
+                         "kernel": "tcgen05 projection GEMMs: linear_tcgen05_pair (QKV, FFN1), linear_ln_cluster "
+                                   "(out-proj + LN), linear_ln_tcgen05_pair (FFN2 + LN)",
+                         "achieved": gemm_tflops, "peak": burst_tf, "unit": "TFLOP/s",
+                         "frac": gemm_tflops / burst_tf, "peak_kind": f"bf16 burst, {peak_kind}",
+                         "frac_of_sustained": gemm_tflops / sustained_tf,
                          "traffic": traffic,
-                         "traffic_note": "DRAM bytes per launch, mean of the four projection GEMMs of one layer "
-                                         "(ncu, profiles/linear_tcgen05_pair_bge-large.md)",
+                         "traffic_note": "DRAM bytes per launch, mean of one layer's four projection launches "
+                                         "(ncu, profiles/projections_bge-large.md)",
                          "gemm_flops_per_step": gemm_flops, "gemm_ms_per_step": gemm_ms / args.steps,
                          "attention": {"bound": "hbm", "achieved": attn_gbs, "peak": hbm_gbs, "unit": "GB/s",
                                        "frac": attn_gbs / hbm_gbs, "tflops": attn_tflops,
-                                       "tensor_frac": attn_tflops / sustained_tf,
+                                       "tensor_frac": attn_tflops / burst_tf,
                                        "ms_per_step": attn_ms / args.steps, "flops_per_step": attn_flops,
                                        "bytes_per_step": attn_bytes},
                          "other_ms_per_step": other_ms / args.steps,
