@@ -339,6 +339,21 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         : "memory");
 }
 
+// True in exactly one lane of a converged warp (elect.sync).  The MMA-issuing warps run
+// their loop on all 32 lanes (the barrier waits and descriptor arithmetic are warp-uniform)
+// and let the elected lane issue each tcgen05.mma / tcgen05.commit: issuing from a lone
+// divergent lane measured about 20 % slower per instruction.
+__device__ __forceinline__ bool elect_lane()
+{
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+        "elect.sync rx|px, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, px;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // Arrives once on `bar` when every tcgen05.mma issued so far by this thread completes.
 __device__ __forceinline__ void umma_commit(uint64_t *bar)
 {

@@ -277,7 +277,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        {
+            const bool leader = elect_lane();  // the whole warp waits; this lane issues
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
             uint32_t qn = 0, kvn = 0, it = 0;
@@ -293,17 +294,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 const uint64_t v_desc = sdesc_sw128(smem_u32(sKV + pks * KV_BYTES + KV_BYTES / 2), TK * 128, 1024);
                 const int nks = (pvalid + 15) >> 4;
                 for (int ks = 0; ks < nks; ++ks)  // each K step advances 16 key rows = 2048 bytes
-                    umma_f16_ts(tmem + b * 128 + 64, tmem + b * 128 + ks * 8, v_desc + static_cast<uint64_t>(ks * 128),
+                    if (leader) umma_f16_ts(tmem + b * 128 + 64, tmem + b * 128 + ks * 8, v_desc + static_cast<uint64_t>(ks * 128),
                                 idesc_o, ks != 0 ? 1u : 0u);
-                umma_commit(&o_full[b]);
-                umma_commit(&v_empty[pks]);
+                if (leader) umma_commit(&o_full[b]);
+                if (leader) umma_commit(&v_empty[pks]);
                 return true;
             };
             for (uint32_t k = 0; ok && !*abort_flag; ++k) {
                 const int slot = k % kRing;
                 if (!(ok = wait(&unit_full[slot], (k / kRing) & 1))) break;
                 const int4 e = ring[slot];
-                mbar_arrive(&unit_empty[slot]);
+                __syncwarp();  // every lane has read the entry before the slot is handed back
+                if (leader) mbar_arrive(&unit_empty[slot]);
                 if (e.y < 0) break;
                 const Unit w = unit_of(e);
                 const int qs = qn % Q_SLOTS;
@@ -321,12 +323,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     const uint64_t k_desc = sdesc_sw128(smem_u32(sKV + ks * KV_BYTES), 16, 1024);
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk)  // each K step advances 32 bytes inside the swizzle atom
-                        umma_f16_ss(tmem + b * 128, q_desc + static_cast<uint64_t>(kk * 2),
+                        if (leader) umma_f16_ss(tmem + b * 128, q_desc + static_cast<uint64_t>(kk * 2),
                                     k_desc + static_cast<uint64_t>(kk * 2), idesc_s, kk != 0 ? 1u : 0u);
                     issued = true;
-                    umma_commit(&s_full[b]);
-                    umma_commit(&k_empty[ks]);
-                    if (j == w.n_kv - 1) umma_commit(&q_empty[qs]);
+                    if (leader) umma_commit(&s_full[b]);
+                    if (leader) umma_commit(&k_empty[ks]);
+                    if (j == w.n_kv - 1 && leader) umma_commit(&q_empty[qs]);
                     if (have_pend && !(ok = issue_pv(pend_it, pend_ks, pend_kvn, pend_valid))) break;
                     have_pend = true;
                     pend_it = it;
@@ -341,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             if (ok && have_pend && !*abort_flag) ok = issue_pv(pend_it, pend_ks, pend_kvn, pend_valid);
             if (issued) {
                 // all MMAs issued by this thread retire before TMEM is released
-                umma_commit(probe);
+                if (leader) umma_commit(probe);
                 (void)mbar_wait_drain(probe, 0);
             }
         }

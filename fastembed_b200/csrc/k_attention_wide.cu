@@ -278,8 +278,10 @@ __global__ void __launch_bounds__(kThreadsW, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ------------------------------------------------ MMA issuer
+        {
+            // ------------------------------------------------ MMA issuer (the whole warp waits; the
+            // elected lane issues)
+            const bool leader = elect_lane();
             constexpr uint32_t idesc_o = idesc_bf16_f32(TQ, HD, false, true);
             uint32_t qn = 0, kvn = 0, it = 0, un = 0;
             bool ok = true, issued = false, have_pend = false;
@@ -297,11 +299,11 @@ __global__ void __launch_bounds__(kThreadsW, 1)
                 const uint32_t o_tmem = tmem + 256 + pend_o * HD;
                 const int nks = (pend_valid + 15) >> 4;
                 for (int ks = 0; ks < nks; ++ks)
-                    umma_f16_ts(o_tmem, tmem + b * 128 + ks * 8, v_desc + static_cast<uint64_t>(ks * 128), idesc_o,
+                    if (leader) umma_f16_ts(o_tmem, tmem + b * 128 + ks * 8, v_desc + static_cast<uint64_t>(ks * 128), idesc_o,
                                 (pend_first && ks == 0) ? 0u : 1u);
-                umma_commit(&pv_done[b]);
-                umma_commit(&s_free[b]);
-                umma_commit(&v_empty[pend_ks]);
+                if (leader) umma_commit(&pv_done[b]);
+                if (leader) umma_commit(&s_free[b]);
+                if (leader) umma_commit(&v_empty[pend_ks]);
                 return true;
             };
             for (int g = blockIdx.x; g < total_units && ok && !*abort_flag; g += gridDim.x) {
@@ -320,14 +322,14 @@ __global__ void __launch_bounds__(kThreadsW, 1)
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk) {  // 4 K steps per 128-byte swizzle atom, then the next box
                         const uint32_t off = (kk >> 2) * BOX_BYTES + (kk & 3) * 32;
-                        umma_f16_ss(tmem + b * 128, sdesc_sw128(smem_u32(sQ + qs * C::TILE) + off, 16, 1024),
+                        if (leader) umma_f16_ss(tmem + b * 128, sdesc_sw128(smem_u32(sQ + qs * C::TILE) + off, 16, 1024),
                                     sdesc_sw128(smem_u32(sK + ks * C::TILE) + off, 16, 1024), idesc_s,
                                     kk != 0 ? 1u : 0u);
                     }
                     issued = true;
-                    umma_commit(&s_full[b]);
-                    umma_commit(&k_empty[ks]);
-                    if (j == w.n_kv - 1) umma_commit(&q_empty[qs]);
+                    if (leader) umma_commit(&s_full[b]);
+                    if (leader) umma_commit(&k_empty[ks]);
+                    if (j == w.n_kv - 1 && leader) umma_commit(&q_empty[qs]);
                     if (have_pend && !(ok = issue_pv())) break;
                     have_pend = true;
                     pend_it = it;
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(kThreadsW, 1)
             }
             if (ok && have_pend && !*abort_flag) ok = issue_pv();
             if (issued) {
-                umma_commit(probe);
+                if (leader) umma_commit(probe);
                 (void)mbar_wait_drain(probe, 0);
             }
         }

@@ -415,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait_drain(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        {
+            const bool leader = elect_lane();  // the whole warp waits; this lane issues
             // ---------------- MMA issuer ----------------
             constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
             int stage = 0;
@@ -444,24 +445,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int k = 0; k < BK / 16; ++k) {
                         const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
                         const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
-                        umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+                        if (leader) umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                     issued = true;
-                    umma_commit(&empty[stage]);
+                    if (leader) umma_commit(&empty[stage]);
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (*abort_flag) break;
-                umma_commit(&acc_full[acc]);
+                if (leader) umma_commit(&acc_full[acc]);
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1;
             }
             if (*abort_flag && issued) {
                 // Let outstanding MMAs retire before TMEM is released.
                 uint64_t *probe = &acc_full[acc];
-                umma_commit(probe);
+                if (leader) umma_commit(probe);
                 if (!mbar_wait_drain(probe, acc_phase)) report(status, DEV_TIMEOUT);
             }
         }
@@ -577,7 +578,7 @@ __device__ __forceinline__ void pair_producer(uint8_t *ring, uint64_t *full, uin
 template <int STAGES>
 __device__ __forceinline__ void pair_mma(uint8_t *ring, uint64_t *full, uint64_t *empty, uint64_t *acc_full,
                                          uint64_t *acc_empty, uint32_t tmem_base, int pair, int npairs, int num_tiles,
-                                         int k_iters, volatile int *abort_flag, int *status)
+                                         int k_iters, volatile int *abort_flag, int *status, bool leader)
 {
     constexpr uint32_t idesc = idesc_bf16_f32(256, P_BN, false, false);
     int stage = 0;
@@ -605,24 +606,24 @@ __device__ __forceinline__ void pair_mma(uint8_t *ring, uint64_t *full, uint64_t
             const uint64_t bd = sdesc_sw128(a_addr + P_HALF_BYTES, 16, 1024);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K step inside the swizzle atom
-                umma_f16_ss_pair(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * 2), idesc,
+                if (leader) umma_f16_ss_pair(d_tmem, ad + static_cast<uint64_t>(k * 2), bd + static_cast<uint64_t>(k * 2), idesc,
                                  (kb | k) != 0 ? 1u : 0u);
             issued = true;
-            umma_commit_pair_both(&empty[stage]);
+            if (leader) umma_commit_pair_both(&empty[stage]);
             if (++stage == STAGES) {
                 stage = 0;
                 phase ^= 1;
             }
         }
         if (*abort_flag) break;
-        umma_commit_pair_both(&acc_full[acc]);
+        if (leader) umma_commit_pair_both(&acc_full[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
     }
     if (*abort_flag && issued) {
         // Let outstanding MMAs retire before TMEM is released.
         uint64_t *probe = &acc_full[acc];
-        umma_commit_pair_both(probe);
+        if (leader) umma_commit_pair_both(probe);
         if (!mbar_wait_drain(probe, acc_phase)) report(status, DEV_TIMEOUT);
     }
 }
@@ -689,9 +690,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
             pair_producer<P_STAGES>(ring, full, empty, &tm_x, &tm_w, rank, pair, npairs, num_tiles, n_tiles, k_iters,
                                     abort_flag, status);
     } else if (warp == 1) {
-        if (lane == 0 && rank == 0)
+        if (rank == 0)  // the whole warp: waits on every lane, MMAs from the elected one
             pair_mma<P_STAGES>(ring, full, empty, acc_full, acc_empty, tmem_base, pair, npairs, num_tiles, k_iters,
-                               abort_flag, status);
+                               abort_flag, status, elect_lane());
     } else {
         // ---------------- epilogue (warps 2.. of both CTAs): warp w drains TMEM lanes
         // 32 * (w % 4) (the lane-quarter rule), columns [h * COLS, (h + 1) * COLS), h = (w - 2) / 4
@@ -891,9 +892,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
             pair_producer<STAGES>(ring, full, empty, &tm_x, &tm_w, rank, pair, npairs, num_tiles, n_tiles, k_iters,
                                   abort_flag, status);
     } else if (warp == 1) {
-        if (lane == 0 && rank == 0)
+        if (rank == 0)  // the whole warp: waits on every lane, MMAs from the elected one
             pair_mma<STAGES>(ring, full, empty, acc_full, acc_empty, tmem_base, pair, npairs, num_tiles, k_iters,
-                             abort_flag, status);
+                             abort_flag, status, elect_lane());
     } else {
         // ---------------- epilogue: warp w drains TMEM lanes 32 * (w % 4) (the lane-quarter
         // rule), accumulator columns [h * COLS, (h + 1) * COLS), h = (w - 2) / 4.
@@ -1593,7 +1594,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait_drain(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        {
+            const bool leader = elect_lane();  // the whole warp waits; this lane issues
             // ---------------- MMA issuer: 128 x 256 per row block, accumulators alternate
             constexpr uint32_t idesc = idesc_bf16_f32(BM, LC_BN, false, false);
             int stage = 0;
@@ -1620,23 +1622,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_addr = a_addr + BM * BK * 2;
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
-                        umma_f16_ss(d_tmem, sdesc_sw128(a_addr + k * 32, 16, 1024), sdesc_sw128(b_addr + k * 32, 16, 1024),
+                        if (leader) umma_f16_ss(d_tmem, sdesc_sw128(a_addr + k * 32, 16, 1024), sdesc_sw128(b_addr + k * 32, 16, 1024),
                                     idesc, (kb | k) != 0 ? 1u : 0u);
                     issued = true;
-                    umma_commit(&empty[stage]);
+                    if (leader) umma_commit(&empty[stage]);
                     if (++stage == LC_STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (*abort_flag) break;
-                umma_commit(&acc_full[acc]);
+                if (leader) umma_commit(&acc_full[acc]);
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1;
             }
             if (*abort_flag && issued) {
                 uint64_t *probe = &acc_full[acc];
-                umma_commit(probe);
+                if (leader) umma_commit(probe);
                 if (!mbar_wait_drain(probe, acc_phase)) report(status, DEV_TIMEOUT);
             }
         }
