@@ -1192,18 +1192,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
     }
 }
 
-// 6 stages x 4 epilogue warps: on the bge-large projections (K = 1024) 5 x 8 and 4 x 8
-// measured 1-5 % slower, the deeper ring mattering more than the wider epilogue.
-constexpr int kPairStages = 6;
-constexpr int kPairEpiWarps = 4;
-
-template <bool OUT_BF16>
-cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N, int K,
-                        const float *bias, const float *residual, int epi, int *status, cudaStream_t s,
-                        const RopeParams &rp)
+// Ring stages x epilogue warps of the pair kernel, by epilogue.  With bias only (or none), 6 x 4:
+// on the bge-large projections (K = 1024) 5 x 8 measured 2-3 % slower, the deeper ring mattering
+// more.  The GELU and gated (SwiGLU / GeGLU) drains cost more arithmetic per element, and with
+// 5 x 8 (two warps per TMEM lane quarter, 128 columns each) FFN1 + GELU went 163.7 -> 158.6 us
+// and the N = 3072 GELU shape 128.8 -> 123.2 us.  The q/k norm + RoPE drain needs a whole
+// head (128 or 256 columns) per warp and stays on four warps.
+template <bool OUT_BF16, int STAGES, int EPI_WARPS>
+cudaError_t launch_pair_cfg(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N, int K,
+                            const float *bias, const float *residual, int epi, int *status, cudaStream_t s,
+                            const RopeParams &rp)
 {
-    using Cfg = PairCfg<kPairStages, kPairEpiWarps>;
-    auto kern = linear_tcgen05_pair<OUT_BF16, kPairStages, kPairEpiWarps>;
+    using Cfg = PairCfg<STAGES, EPI_WARPS>;
+    auto kern = linear_tcgen05_pair<OUT_BF16, STAGES, EPI_WARPS>;
     static uint64_t configured[64] = {};  // context the attribute was set in
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1219,6 +1220,16 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
     if (pairs < 1) pairs = 1;
     return launch_k(kern, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, s, tx, tw, ty, M, N, K, bias, residual,
                     epi, status, rp);
+}
+
+template <bool OUT_BF16>
+cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N, int K,
+                        const float *bias, const float *residual, int epi, int *status, cudaStream_t s,
+                        const RopeParams &rp)
+{
+    if (epi == E_GELU || epi == E_SWIGLU || epi == E_GEGLU)
+        return launch_pair_cfg<OUT_BF16, 5, 8>(tx, tw, ty, M, N, K, bias, residual, epi, status, s, rp);
+    return launch_pair_cfg<OUT_BF16, 6, 4>(tx, tw, ty, M, N, K, bias, residual, epi, status, s, rp);
 }
 
 // Pairs of linear_ln_tcgen05_pair<Cfg> that can be resident at once on the current
