@@ -187,10 +187,17 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
 {
     if constexpr (OUT_BF16) {
         if (epi == E_QKROPE) {
+            // a warp drains whole heads: 128-column warps (the 8-warp pair kernel) take head_dim 128
+            // only, and the launcher gives them no other
             if constexpr (BN >= 256) {
                 if (n0 < rp.k_end) {
                     if (rp.hd == 128) drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
                     else drain_qk_rope<BN, 256>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
+                    return;
+                }
+            } else if constexpr (BN == 128) {
+                if (n0 < rp.k_end && rp.hd == 128) {
+                    drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
                     return;
                 }
             }
@@ -1196,8 +1203,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
 // on the bge-large projections (K = 1024) 5 x 8 measured 2-3 % slower, the deeper ring mattering
 // more.  The GELU and gated (SwiGLU / GeGLU) drains cost more arithmetic per element, and with
 // 5 x 8 (two warps per TMEM lane quarter, 128 columns each) FFN1 + GELU went 163.7 -> 158.6 us
-// and the N = 3072 GELU shape 128.8 -> 123.2 us.  The q/k norm + RoPE drain needs a whole
-// head (128 or 256 columns) per warp and stays on four warps.
+// and the N = 3072 GELU shape 128.8 -> 123.2 us.  The q/k norm + RoPE drain needs a whole head
+// per warp: head_dim 128 takes the 8-warp form (Qwen3 QKV 472.6 -> 468.4 us), head_dim 256
+// stays on four warps.
 template <bool OUT_BF16, int STAGES, int EPI_WARPS>
 cudaError_t launch_pair_cfg(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, int M, int N, int K,
                             const float *bias, const float *residual, int epi, int *status, cudaStream_t s,
@@ -1227,7 +1235,7 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
                         const float *bias, const float *residual, int epi, int *status, cudaStream_t s,
                         const RopeParams &rp)
 {
-    if (epi == E_GELU || epi == E_SWIGLU || epi == E_GEGLU)
+    if (epi == E_GELU || epi == E_SWIGLU || epi == E_GEGLU || (epi == E_QKROPE && rp.hd == 128))
         return launch_pair_cfg<OUT_BF16, 5, 8>(tx, tw, ty, M, N, K, bias, residual, epi, status, s, rp);
     return launch_pair_cfg<OUT_BF16, 6, 4>(tx, tw, ty, M, N, K, bias, residual, epi, status, s, rp);
 }
