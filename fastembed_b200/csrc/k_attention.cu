@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         mbar_init(probe, 1);
         for (int i = 0; i < kRing; ++i) {
             mbar_init(&unit_full[i], 1);
-            mbar_init(&unit_empty[i], 5);  // the MMA thread and one arrival per softmax warp
+            mbar_init(&unit_empty[i], 5);  // one arrival from the MMA warp and one per softmax warp
         }
         *abort_flag = 0;
         fence_mbar_init();

@@ -8,7 +8,7 @@
 // CTAs in flight share each 128-row block of x through L2):
 //   warp 0      TMA producer: x tile [128 x 64] and W tile [BN x 64] per stage into
 //               a STAGES-deep ring of 128B-swizzled shared-memory buffers.
-//   warp 1      TMEM owner and MMA issuer: one thread issues tcgen05.mma
+//   warp 1      TMEM owner and MMA issuer: the warp waits, one elected lane issues tcgen05.mma
 //               (M=128, N=BN, K=16) x 4 per stage into one of two TMEM accumulators,
 //               tcgen05.commit frees the smem stage / publishes the accumulator.
 //   warps 2-5   epilogue: each warp drains its 32 TMEM lanes (= 32 rows) with
@@ -580,7 +580,7 @@ __device__ __forceinline__ void pair_producer(uint8_t *ring, uint64_t *full, uin
                 if (!mbar_wait_drain(&full[s], (armed_parity >> s) & 1u)) report(status, DEV_TIMEOUT);
 }
 
-// MMA issuer of a pair (lane 0 of warp 1 in the leader): 256 x 256 x 64 per stage
+// MMA issuer of a pair (warp 1 of the leader; its elected lane issues): 256 x 256 x 64 per stage
 // into one of two TMEM accumulators.
 template <int STAGES>
 __device__ __forceinline__ void pair_mma(uint8_t *ring, uint64_t *full, uint64_t *empty, uint64_t *acc_full,
