@@ -20,10 +20,15 @@
 //              the upper 64 columns of P's slot.
 //   warps 2-5  softmax: thread = query row; reads its S row (tcgen05.ld), masks keys past
 //              the sentence end, online max / sum, writes P (bf16) back over the first 64
-//              columns (tcgen05.st); one item later folds O into fp32 registers and,
-//              after a unit's last item, stores O / l.  (Folding O first would free the
-//              slot for the next S earlier, but then waits for this item's PV instead:
-//              measured slower with two slots per CTA.)
+//              columns (tcgen05.st) and the row's rescale factor and running sum into
+//              shared memory.
+//   warps 6-9  O fold: thread = query row; once an item's PV is done, reads its 64 O
+//              columns from TMEM into fp32 registers (o = o * alpha + O), hands the slot
+//              back to the MMA warp, and after a unit's last item stores O / l.
+// A slot turns over as S -> softmax -> PV -> fold.  With the fold on warps of its own, the
+// softmax warps go on to the other slot's S while this slot's PV and fold run, so neither
+// the S latency nor the fold sits between two softmax passes (when the softmax warps also
+// folded, each item cost the S latency + softmax + fold in a row).
 // K and V tiles have separate full / empty barriers: a K slot is reloaded as soon as
 // the S two items back is done with it, without waiting for that item's PV.
 // Waits are bounded; on timeout the CTA records FE_ERR_DEVICE_TIMEOUT, drains what it
@@ -44,18 +49,28 @@ constexpr int TQ = 128;
 constexpr int TK = 128;
 constexpr int Q_SLOTS = 2;
 constexpr int KV_SLOTS = 2;
-constexpr int kLookahead = 4;                   // units grabbed ahead of the loads
-constexpr int kRing = 8;                        // grabbed units in flight to the MMA and softmax warps
+constexpr int kLookahead = 2;                   // units grabbed ahead of the loads
+constexpr int kRing = 8;                        // grabbed units in flight to the MMA, softmax and fold warps
 constexpr int kMaxBatch = 2048;                 // sentences per launch (prefix table in shared memory)
 constexpr int kCtasPerSm = 2;
 constexpr int kSchedSlots = 64;                 // work counters, one per launch in flight
 constexpr uint32_t Q_BYTES = TQ * HD * 2;       // 16 KB
 constexpr uint32_t KV_BYTES = 2 * TK * HD * 2;  // K then V, 32 KB
 constexpr uint32_t BAR_BYTES = 512;
+constexpr uint32_t ROW_BYTES = 2 * 2 * TQ * 4;  // per slot and query row: rescale factor, running sum
 constexpr uint32_t SMEM_BYTES =
-    1024 + Q_SLOTS * Q_BYTES + KV_SLOTS * KV_BYTES + BAR_BYTES + 16 * kRing + 4 * (kMaxBatch + 1) + 64;
+    1024 + Q_SLOTS * Q_BYTES + KV_SLOTS * KV_BYTES + BAR_BYTES + 16 * kRing + ROW_BYTES + 4 * (kMaxBatch + 1) + 64;
 constexpr uint32_t TMEM_COLS = 256;  // two slots: S [0,128) -> P [0,64) + O [64,128)
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+
+// 32 lanes x 32 bit, 8 consecutive columns: thread i of the warp receives lane
+// (lane base of taddr + i), columns [col, col + 8).
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
 
 __device__ __forceinline__ float fast_exp2(float x)
 {
@@ -107,13 +122,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     uint64_t *slot_free = o_full + 2;         // [2] O of a slot consumed
     uint64_t *probe = slot_free + 2;          // [1]
     uint64_t *unit_full = probe + 1;          // [kRing] a grabbed unit is in the ring slot
-    uint64_t *unit_empty = unit_full + kRing; // [kRing] the MMA and softmax warps have read it
+    uint64_t *unit_empty = unit_full + kRing; // [kRing] the MMA, softmax and fold warps have read it
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(unit_empty + kRing);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     int *warp_tot = reinterpret_cast<int *>(tmem_slot + 2);  // [kThreads / 32]
     // ring entries are written before an mbarrier arrive and read after the matching wait
     int4 *ring = reinterpret_cast<int4 *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES);
-    int *upre = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES + 16 * kRing);  // [batch + 1]
+    // per slot and query row, written by the softmax warp before its p_full arrive and read
+    // by the fold warp after waiting on the same p_full phase
+    float *row_alpha = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES + 16 * kRing);  // [2][TQ]
+    float *row_l = row_alpha + 2 * TQ;                                                                     // [2][TQ]
+    int *upre = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES + 16 * kRing + ROW_BYTES);  // [batch + 1]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -134,12 +153,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 4);     // one arrival per softmax warp
             mbar_init(&o_full[i], 1);
-            mbar_init(&slot_free[i], 4);  // one arrival per softmax warp
+            mbar_init(&slot_free[i], 4);  // one arrival per fold warp
         }
         mbar_init(probe, 1);
         for (int i = 0; i < kRing; ++i) {
             mbar_init(&unit_full[i], 1);
-            mbar_init(&unit_empty[i], 5);  // one arrival from the MMA warp and one per softmax warp
+            mbar_init(&unit_empty[i], 9);  // one arrival from the MMA warp, one per softmax and fold warp
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -205,17 +224,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (warp == 0) {
         if (lane == 0) {
             // ------------------------------------------------ TMA producer + unit scheduler
-            uint32_t qn = 0, kvn = 0;
-            uint32_t q_armed = 0, kv_armed = 0, q_par = 0, kv_par = 0;  // kv_*: the K and V loads of a slot
+            // Loads run in the order the MMA warp consumes them: a unit's Q, then per item its
+            // K followed by the previous item's V (whose PV is issued after this item's S), so
+            // neither the next K nor the next unit's Q waits behind a V slot.
+            uint32_t qn = 0, kn = 0, vn = 0;
+            uint32_t q_armed = 0, k_armed = 0, v_armed = 0, q_par = 0, k_par = 0, v_par = 0;
             bool ok = true;
             uint32_t grabbed = 0, loaded = 0;  // units pushed into the ring / whose tiles were loaded
             bool grab_done = false;
-            // Takes the next unit of the launch (or, past the last one, the end marker),
+            // The next unit index is fetched one grab ahead, so the atomic's round trip
+            // overlaps the loads instead of delaying the next unit's Q.
+            unsigned ticket = atomicAdd(&sched[0], 1u);
+            // Takes the ticketed unit of the launch (or, past the last one, the end marker),
             // pushes it into the ring.
             auto grab = [&]() -> bool {
-                const unsigned g = atomicAdd(&sched[0], 1u);
+                const unsigned g = ticket;
                 int4 e = make_int4(0, -1, 0, 0);
                 if (g < total_units) {
+                    ticket = atomicAdd(&sched[0], 1u);
                     int lo = 0, hi = batch - 1;  // last sentence s with upre[s] <= g
                     while (lo < hi) {
                         const int mid = (lo + hi + 1) >> 1;
@@ -234,6 +260,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 if (e.y < 0) grab_done = true;
                 return true;
             };
+            // V of item vn (head, first key row) into the V half of its K/V slot
+            auto load_v = [&](int head, int row) -> bool {
+                const int vs = vn % KV_SLOTS;
+                if (!wait(&v_empty[vs], ((vn / KV_SLOTS) & 1) ^ 1)) return false;
+                mbar_arrive_expect_tx(&v_full[vs], KV_BYTES / 2);
+                load_tile(sKV + vs * KV_BYTES + KV_BYTES / 2, &v_full[vs], 2, head, row);
+                v_armed |= 1u << vs;
+                v_par = (v_par & ~(1u << vs)) | (((vn / KV_SLOTS) & 1) << vs);
+                ++vn;
+                return true;
+            };
+            bool have_v = false;
+            int v_head = 0, v_row = 0;
             while (ok && !*abort_flag) {
                 while (ok && !grab_done && grabbed < loaded + kLookahead) ok = grab();
                 if (!ok || loaded == grabbed) break;
@@ -249,32 +288,29 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 q_par = (q_par & ~(1u << qs)) | (((qn / Q_SLOTS) & 1) << qs);
                 ++qn;
                 for (int j = 0; j < w.n_kv; ++j) {
-                    // K as soon as the S of two items back is done with the slot; V once its PV is
-                    const int ks = kvn % KV_SLOTS;
-                    const uint32_t par = ((kvn / KV_SLOTS) & 1) ^ 1;
-                    uint8_t *dst = sKV + ks * KV_BYTES;
-                    if (!(ok = wait(&k_empty[ks], par))) break;
+                    // K as soon as the S of two items back is done with the slot
+                    const int ks = kn % KV_SLOTS;
+                    if (!(ok = wait(&k_empty[ks], ((kn / KV_SLOTS) & 1) ^ 1))) break;
                     mbar_arrive_expect_tx(&k_full[ks], KV_BYTES / 2);
-                    load_tile(dst, &k_full[ks], 1, w.head, w.start + j * TK);
-                    if (!(ok = wait(&v_empty[ks], par))) {
-                        (void)mbar_wait_drain(&k_full[ks], par ^ 1);  // the K load just started lands first
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&v_full[ks], KV_BYTES / 2);
-                    load_tile(dst + KV_BYTES / 2, &v_full[ks], 2, w.head, w.start + j * TK);
-                    kv_armed |= 1u << ks;
-                    kv_par = (kv_par & ~(1u << ks)) | (((kvn / KV_SLOTS) & 1) << ks);
-                    ++kvn;
+                    load_tile(sKV + ks * KV_BYTES, &k_full[ks], 1, w.head, w.start + j * TK);
+                    k_armed |= 1u << ks;
+                    k_par = (k_par & ~(1u << ks)) | (((kn / KV_SLOTS) & 1) << ks);
+                    ++kn;
+                    // then the previous item's V, once the PV two items back is done with its slot
+                    if (have_v && !(ok = load_v(v_head, v_row))) break;
+                    have_v = true;
+                    v_head = w.head;
+                    v_row = w.start + j * TK;
                 }
             }
+            if (ok && have_v && !*abort_flag) (void)load_v(v_head, v_row);
             // every load this thread started lands before the CTA exits
             for (int i = 0; i < Q_SLOTS; ++i)
                 if ((q_armed >> i) & 1) (void)mbar_wait_drain(&q_full[i], (q_par >> i) & 1);
-            for (int i = 0; i < KV_SLOTS; ++i)
-                if ((kv_armed >> i) & 1) {
-                    (void)mbar_wait_drain(&k_full[i], (kv_par >> i) & 1);
-                    (void)mbar_wait_drain(&v_full[i], (kv_par >> i) & 1);
-                }
+            for (int i = 0; i < KV_SLOTS; ++i) {
+                if ((k_armed >> i) & 1) (void)mbar_wait_drain(&k_full[i], (k_par >> i) & 1);
+                if ((v_armed >> i) & 1) (void)mbar_wait_drain(&v_full[i], (v_par >> i) & 1);
+            }
         }
     } else if (warp == 1) {
         {
@@ -347,60 +383,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 (void)mbar_wait_drain(probe, 0);
             }
         }
-    } else {
+    } else if (warp < 6) {
         // ------------------------------------------------ softmax warps 2..5
         const int q = warp & 3;
         const int r = q * 32 + lane;  // query row within the tile == TMEM lane
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        float o[HD];
-#pragma unroll
-        for (int d = 0; d < HD; ++d) o[d] = 0.f;
         uint32_t it = 0;
-        bool ok = true, have_pend = false;
-        uint32_t pend_it = 0;
-        float pend_alpha = 0.f, pend_l = 1.f;
-        bool pend_last = false, pend_live = false;
-        __nv_bfloat16 *pend_dst = nullptr;
-
-        auto consume = [&](uint32_t pit, float alpha, bool last, float l, __nv_bfloat16 *dst, bool live) -> bool {
-            const uint32_t b = pit & 1;
-            if (!wait(&o_full[b], (pit >> 1) & 1)) return false;
-            if (live) {
-                tc_fence_after();
-                uint32_t v0[32], v1[32];
-                const uint32_t tO = tmem + lane_base + b * 128 + 64;
-                tmem_ld_x32(tO, v0);
-                tmem_ld_x32(tO + 32, v1);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    o[i] = o[i] * alpha + __uint_as_float(v0[i]);
-                    o[32 + i] = o[32 + i] * alpha + __uint_as_float(v1[i]);
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&slot_free[b]);
-            if (live && last) {
-                if (dst) {
-                    const float inv = 1.0f / l;
-                    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-#pragma unroll
-                    for (int x = 0; x < HD / 8; ++x) {
-                        uint4 wv;
-                        wv.x = pack_bf16x2(o[x * 8 + 0] * inv, o[x * 8 + 1] * inv);
-                        wv.y = pack_bf16x2(o[x * 8 + 2] * inv, o[x * 8 + 3] * inv);
-                        wv.z = pack_bf16x2(o[x * 8 + 4] * inv, o[x * 8 + 5] * inv);
-                        wv.w = pack_bf16x2(o[x * 8 + 6] * inv, o[x * 8 + 7] * inv);
-                        d4[x] = wv;
-                    }
-                }
-#pragma unroll
-                for (int d = 0; d < HD; ++d) o[d] = 0.f;
-            }
-            return true;
-        };
-
+        bool ok = true;
         for (uint32_t k = 0; ok; ++k) {
             if (*abort_flag) break;
             const int slot = k % kRing;
@@ -411,12 +400,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             if (e.y < 0) break;
             const Unit w = unit_of(e);
             float m_run = -INFINITY, l_run = 0.f;
-            __nv_bfloat16 *dst = nullptr;
-            if (w.q0 + r < w.len) {
-                const size_t row = static_cast<size_t>(w.start + w.q0 + r);
-                dst = head_major ? out + (static_cast<size_t>(w.head) * total_tokens + row) * HD
-                                 : out + row * dim + w.head * HD;
-            }
             // A warp whose 32 query rows all lie past the sentence end does no softmax work:
             // its P and O rows are never read back (each O row depends only on its P row).
             const bool warp_live = w.q0 + q * 32 < w.len;
@@ -477,26 +460,83 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     }
                     tmem_wait_st();
                 }
+                l_run = l_run * alpha + (rs0 + rs1);
+                m_run = mx;
+                row_alpha[b * TQ + r] = alpha;
+                row_l[b * TQ + r] = l_run;
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[b]);
-                l_run = l_run * alpha + (rs0 + rs1);
-                m_run = mx;
-                if (have_pend && !(ok = consume(pend_it, pend_alpha, pend_last, pend_l, pend_dst, pend_live))) break;
-                have_pend = true;
-                pend_it = it;
-                pend_alpha = alpha;
-                pend_last = j == w.n_kv - 1;
-                pend_l = l_run;
-                pend_dst = dst;
-                pend_live = warp_live;
                 ++it;
             }
         }
-        if (ok && have_pend && !*abort_flag)
-            (void)consume(pend_it, pend_alpha, pend_last, pend_l, pend_dst, pend_live);
+    } else {
+        // ------------------------------------------------ O fold warps 6..9
+        const int q = warp & 3;
+        const int r = q * 32 + lane;  // query row within the tile == TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        float o[HD];
+#pragma unroll
+        for (int d = 0; d < HD; ++d) o[d] = 0.f;
+        uint32_t it = 0;
+        bool ok = true;
+        for (uint32_t k = 0; ok; ++k) {
+            if (*abort_flag) break;
+            const int slot = k % kRing;
+            if (!(ok = wait(&unit_full[slot], (k / kRing) & 1))) break;
+            const int4 e = ring[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&unit_empty[slot]);
+            if (e.y < 0) break;
+            const Unit w = unit_of(e);
+            __nv_bfloat16 *dst = nullptr;
+            if (w.q0 + r < w.len) {
+                const size_t row = static_cast<size_t>(w.start + w.q0 + r);
+                dst = head_major ? out + (static_cast<size_t>(w.head) * total_tokens + row) * HD
+                                 : out + row * dim + w.head * HD;
+            }
+            const bool warp_live = w.q0 + q * 32 < w.len;  // the same rows the softmax warp skips
+            for (int j = 0; j < w.n_kv; ++j) {
+                const uint32_t b = it & 1;
+                const uint32_t par = (it >> 1) & 1;
+                if (!(ok = wait(&o_full[b], par))) break;
+                if (warp_live) {
+                    // p_full of this phase has completed (PV waited for it); waiting on it
+                    // here orders the reads of the softmax warp's row values
+                    if (!(ok = wait(&p_full[b], par))) break;
+                    const float alpha = row_alpha[b * TQ + r];
+                    const float inv = 1.0f / row_l[b * TQ + r];
+                    const bool store = dst != nullptr && j == w.n_kv - 1;
+                    tc_fence_after();
+                    const uint32_t tO = tmem + lane_base + b * 128 + 64;
+#pragma unroll
+                    for (int c = 0; c < HD; c += 8) {  // 8 columns per load: o[64] stays in registers
+                        uint32_t v[8];
+                        tmem_ld_x8(tO + c, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) o[c + i] = o[c + i] * alpha + __uint_as_float(v[i]);
+                        if (store) {  // O / l of the unit's last item, 8 columns at a time
+                            uint4 wv;
+                            wv.x = pack_bf16x2(o[c + 0] * inv, o[c + 1] * inv);
+                            wv.y = pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
+                            wv.z = pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv);
+                            wv.w = pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv);
+                            *reinterpret_cast<uint4 *>(dst + c) = wv;
+                        }
+                    }
+                    if (j == w.n_kv - 1) {
+#pragma unroll
+                        for (int d = 0; d < HD; ++d) o[d] = 0.f;
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&slot_free[b]);
+                ++it;
+            }
+        }
     }
-
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
