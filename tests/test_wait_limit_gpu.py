@@ -42,6 +42,35 @@ def test_wait_runs_out_then_recovers(cuda_dev):
     assert torch.equal(after, before)
 
 
+def test_attention_wait_runs_out_then_recovers(cuda_dev):
+    """The head_dim-64 attention under a 1 microsecond wait limit: a fold warp's first wait
+    for its O spans the first item's K load, S, softmax and PV, so it runs out.  Every role
+    leaves its loop, the producer and the S / PV issuer drain what they started, the CTA
+    releases its TMEM, and the launch's work counter is reset by its last CTA: the next
+    call, with the default limit, gives the same bits as a call made before."""
+    import numpy as np
+    from fastembed_b200 import capi, ops
+    L = capi.lib()
+    lens = [96, 300, 17, 128, 512, 64] * 8
+    g = torch.Generator(device=cuda_dev).manual_seed(12)
+    qkv = torch.randn(sum(lens), 3 * 16 * 64, device=cuda_dev, generator=g).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    before = ops.attention_varlen(qkv, cu, max(lens), 16)
+    torch.cuda.synchronize()
+    assert L.fe_device_status(0) == 0
+    assert L.fe_set_wait_limit(0, 1000) == 0
+    try:
+        ops.attention_varlen(qkv, cu, max(lens), 16)
+        st = L.fe_device_status(0)
+    finally:
+        assert L.fe_set_wait_limit(0, DEFAULT_NS) == 0
+    assert st == TIMEOUT, capi.STATUS.get(st, st)
+    after = ops.attention_varlen(qkv, cu, max(lens), 16)
+    torch.cuda.synchronize()
+    assert L.fe_device_status(0) == 0
+    assert torch.equal(after, before)
+
+
 def test_wait_limit_rejects_bad_arguments(cuda_dev):
     from fastembed_b200 import capi
     assert capi.lib().fe_set_wait_limit(0, 0) == 1  # FE_ERR_INVALID_ARGUMENT
