@@ -89,6 +89,11 @@ _SIGS = {
     "fe_rms_sandwich": ([vp, vp, vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),
     "fe_rms_sandwich_bf16": ([vp, vp, vp, vp, i32, f32, i64, i32, vp, vp, vp], C.c_int),
     "fe_linear_qk_norm_rope_bf16": ([vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, f32, f32, vp], C.c_int),
+    "fe_linear_qk_norm_rope_scaled_bf16": ([vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, f32, f32, vp, i32,
+                                            vp], C.c_int),
+    "fe_linear_rmsnorm_deferred_bf16": ([vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp], C.c_int),
+    "fe_linear_rmsnorm_deferred_parts": ([i64], C.c_int32),
+    "fe_linear_row_scaled_bf16": ([vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, C.c_int, vp, i32, f32, vp], C.c_int),
     "fe_token_positions": ([vp, i32, vp, vp], C.c_int),
     "fe_qk_norm_rope_bf16": ([vp, vp, i32, i64, i32, i32, i32, vp, vp, i32, f32, f32, vp], C.c_int),
     "fe_pool_l2": ([vp, vp, i32, i32, C.c_int, vp, vp], C.c_int),

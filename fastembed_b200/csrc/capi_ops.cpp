@@ -128,36 +128,53 @@ fe_status fe_mha_f32(const float *x, const float *wq, const float *wk, const flo
     return done(fe::launch_mha_core_f32(q, k, v, out, seq_len, dim, heads, s), "fe_mha_f32");
 }
 
+static fe_status linear_call(const char *name, const void *x, const void *w, const float *bias, const float *residual,
+                             void *y, int64_t m, int64_t n, int64_t k, fe_epilogue epilogue, fe_dtype y_dtype,
+                             const float *row_ss, int32_t ss_parts, float ss_eps, fe_stream_t stream)
+{
+    if (m < 0 || n <= 0 || k <= 0) return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": bad shape");
+    if (k % 8 != 0 || n % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": k and n must be multiples of 8");
+    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, std::string(name) + ": size too large");
+    if (epilogue < FE_EPI_NONE || epilogue > FE_EPI_GEGLU)
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": unknown epilogue");
+    const bool glu = epilogue == FE_EPI_SWIGLU || epilogue == FE_EPI_GEGLU;
+    if (glu && (n % 128 != 0 || y_dtype != FE_DTYPE_BF16))
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": gated epilogues need n % 128 == 0 and bf16 output");
+    if (y_dtype != FE_DTYPE_F32 && y_dtype != FE_DTYPE_BF16)
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": unknown output dtype");
+    if (epilogue == FE_EPI_BIAS_RESIDUAL && y_dtype != FE_DTYPE_F32)
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": the residual epilogue writes fp32");
+    if (m == 0) return FE_OK;
+    if (!x || !w || !y) return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+    if (epilogue != FE_EPI_NONE && !glu && !bias)
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": epilogue needs a bias");
+    if (epilogue == FE_EPI_BIAS_RESIDUAL && !residual)
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": residual epilogue needs a residual");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias && !aligned16(bias)) ||
+        (residual && !aligned16(residual)))
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": pointers must be 16-byte aligned");
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_linear_bf16(x, w, bias, residual, y, m, n, k, epilogue, y_dtype,
+                                           reinterpret_cast<cudaStream_t>(stream), &st, row_ss, ss_parts, ss_eps);
+    if (st != FE_OK) return st;
+    return done(e, name);
+}
+
 fe_status fe_linear_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
                          int64_t m, int64_t n, int64_t k, fe_epilogue epilogue, fe_dtype y_dtype,
                          fe_stream_t stream)
 {
-    if (m < 0 || n <= 0 || k <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: bad shape");
-    if (k % 8 != 0 || n % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: k and n must be multiples of 8");
-    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_linear_bf16: size too large");
-    if (epilogue < FE_EPI_NONE || epilogue > FE_EPI_GEGLU)
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: unknown epilogue");
-    const bool glu = epilogue == FE_EPI_SWIGLU || epilogue == FE_EPI_GEGLU;
-    if (glu && (n % 128 != 0 || y_dtype != FE_DTYPE_BF16))
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: gated epilogues need n % 128 == 0 and bf16 output");
-    if (y_dtype != FE_DTYPE_F32 && y_dtype != FE_DTYPE_BF16)
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: unknown output dtype");
-    if (epilogue == FE_EPI_BIAS_RESIDUAL && y_dtype != FE_DTYPE_F32)
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: the residual epilogue writes fp32");
-    if (m == 0) return FE_OK;
-    if (!x || !w || !y) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: null pointer");
-    if (epilogue != FE_EPI_NONE && !glu && !bias)
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: epilogue needs a bias");
-    if (epilogue == FE_EPI_BIAS_RESIDUAL && !residual)
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: residual epilogue needs a residual");
-    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias && !aligned16(bias)) ||
-        (residual && !aligned16(residual)))
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_bf16: pointers must be 16-byte aligned");
-    fe_status st = FE_OK;
-    cudaError_t e = fe::launch_linear_bf16(x, w, bias, residual, y, m, n, k, epilogue, y_dtype,
-                                           reinterpret_cast<cudaStream_t>(stream), &st);
-    if (st != FE_OK) return st;
-    return done(e, "fe_linear_bf16");
+    return linear_call("fe_linear_bf16", x, w, bias, residual, y, m, n, k, epilogue, y_dtype, nullptr, 0, 0.f, stream);
+}
+
+fe_status fe_linear_row_scaled_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
+                                    int64_t m, int64_t n, int64_t k, fe_epilogue epilogue, fe_dtype y_dtype,
+                                    const float *row_ss, int32_t ss_parts, float eps, fe_stream_t stream)
+{
+    if (ss_parts < 1 || ss_parts > 8) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_row_scaled_bf16: ss_parts must be 1..8");
+    if (m > 0 && !row_ss) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_row_scaled_bf16: null pointer");
+    return linear_call("fe_linear_row_scaled_bf16", x, w, bias, residual, y, m, n, k, epilogue, y_dtype, row_ss, ss_parts,
+                       eps, stream);
 }
 
 fe_status fe_attention_varlen_bf16(const void *qkv, const int32_t *cu_seqlens, int32_t batch, int32_t max_len,
@@ -320,6 +337,33 @@ fe_status fe_linear_rmsnorm_bf16(const void *x, const void *w, const float *bias
     return done(e, "fe_linear_rmsnorm_bf16");
 }
 
+int32_t fe_linear_rmsnorm_deferred_parts(int64_t n)
+{
+    return n > 0 && n % 256 == 0 && n <= 2048 ? fe::linear_rms_deferred_parts(n) : 0;
+}
+
+fe_status fe_linear_rmsnorm_deferred_bf16(const void *x, const void *w, const float *bias, const float *rms_w,
+                                          float *h32, void *h16, float *row_ss, int64_t m, int64_t n, int64_t k,
+                                          fe_stream_t stream)
+{
+    if (m < 0 || n <= 0 || k <= 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_deferred_bf16: bad shape");
+    if (k % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_deferred_bf16: k must be a multiple of 8");
+    if (n % 256 != 0 || n > 2048)
+        return fail(FE_ERR_UNSUPPORTED, "fe_linear_rmsnorm_deferred_bf16: n must be a multiple of 256, at most 2048");
+    if (m > 0x7fffffff || k > 0x7fffffff) return fail(FE_ERR_UNSUPPORTED, "fe_linear_rmsnorm_deferred_bf16: size too large");
+    if (m == 0) return FE_OK;
+    if (!x || !w || !bias || !rms_w || !h32 || !row_ss)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_deferred_bf16: null pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(bias) || !aligned16(rms_w) || !aligned16(h32) ||
+        (h16 && !aligned16(h16)) || !aligned16(row_ss))
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_rmsnorm_deferred_bf16: pointers must be 16-byte aligned");
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_linear_rms_deferred(x, w, bias, rms_w, h32, h16, row_ss, m, n, k,
+                                                   reinterpret_cast<cudaStream_t>(stream), &st);
+    if (st != FE_OK) return st;
+    return done(e, "fe_linear_rmsnorm_deferred_bf16");
+}
+
 static bool rms_dim_ok(int32_t dim) { return supported_row_dim(dim) && dim != 128; }
 
 fe_status fe_embed_scale(const int32_t *ids, int64_t total_tokens, const float *word, int32_t vocab, int32_t dim,
@@ -388,32 +432,54 @@ fe_status fe_qk_norm_rope_bf16(void *qkv, const int32_t *cu_seqlens, int32_t bat
                 "fe_qk_norm_rope_bf16");
 }
 
+static fe_status qk_norm_rope_call(const char *name, const void *x, const void *w, const float *q_w, const float *k_w,
+                                   const int32_t *positions, void *qkv, int64_t m, int64_t k, int32_t q_heads,
+                                   int32_t kv_heads, int32_t head_dim, int32_t one_plus, float eps, float theta,
+                                   const float *row_ss, int32_t ss_parts, fe_stream_t stream)
+{
+    if (m < 0 || k <= 0 || q_heads <= 0 || kv_heads <= 0 || !(theta > 1.0f))
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": bad shape");
+    if (k % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": k must be a multiple of 8");
+    if (head_dim != 128 && head_dim != 256)
+        return fail(FE_ERR_UNSUPPORTED, std::string(name) + ": head_dim must be 128 or 256");
+    if ((static_cast<int64_t>(q_heads) * head_dim) % 256 != 0 || (static_cast<int64_t>(kv_heads) * head_dim) % 256 != 0)
+        return fail(FE_ERR_UNSUPPORTED,
+                    std::string(name) + ": q_heads * head_dim and kv_heads * head_dim must be multiples of 256");
+    if (m > 0x7fffffff || k > 0x7fffffff || static_cast<int64_t>(q_heads + 2 * kv_heads) * head_dim > 0x7fffffff)
+        return fail(FE_ERR_UNSUPPORTED, std::string(name) + ": size too large");
+    if (m == 0) return FE_OK;
+    if (!x || !w || !q_w || !k_w || !positions || !qkv)
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(qkv))
+        return fail(FE_ERR_INVALID_ARGUMENT, std::string(name) + ": pointers must be 16-byte aligned");
+    fe_status st = FE_OK;
+    cudaError_t e = fe::launch_linear_qk_norm_rope(x, w, qkv, m, k, q_heads, kv_heads, head_dim, q_w, k_w, positions,
+                                                   one_plus != 0, eps, theta, reinterpret_cast<cudaStream_t>(stream),
+                                                   &st, row_ss, ss_parts);
+    if (st != FE_OK) return st;
+    return done(e, name);
+}
+
 fe_status fe_linear_qk_norm_rope_bf16(const void *x, const void *w, const float *q_w, const float *k_w,
                                       const int32_t *positions, void *qkv, int64_t m, int64_t k, int32_t q_heads,
                                       int32_t kv_heads, int32_t head_dim, int32_t one_plus, float eps, float theta,
                                       fe_stream_t stream)
 {
-    if (m < 0 || k <= 0 || q_heads <= 0 || kv_heads <= 0 || !(theta > 1.0f))
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: bad shape");
-    if (k % 8 != 0) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: k must be a multiple of 8");
-    if (head_dim != 128 && head_dim != 256)
-        return fail(FE_ERR_UNSUPPORTED, "fe_linear_qk_norm_rope_bf16: head_dim must be 128 or 256");
-    if ((static_cast<int64_t>(q_heads) * head_dim) % 256 != 0 || (static_cast<int64_t>(kv_heads) * head_dim) % 256 != 0)
-        return fail(FE_ERR_UNSUPPORTED,
-                    "fe_linear_qk_norm_rope_bf16: q_heads * head_dim and kv_heads * head_dim must be multiples of 256");
-    if (m > 0x7fffffff || k > 0x7fffffff || static_cast<int64_t>(q_heads + 2 * kv_heads) * head_dim > 0x7fffffff)
-        return fail(FE_ERR_UNSUPPORTED, "fe_linear_qk_norm_rope_bf16: size too large");
-    if (m == 0) return FE_OK;
-    if (!x || !w || !q_w || !k_w || !positions || !qkv)
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: null pointer");
-    if (!aligned16(x) || !aligned16(w) || !aligned16(qkv))
-        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_bf16: pointers must be 16-byte aligned");
-    fe_status st = FE_OK;
-    cudaError_t e = fe::launch_linear_qk_norm_rope(x, w, qkv, m, k, q_heads, kv_heads, head_dim, q_w, k_w, positions,
-                                                   one_plus != 0, eps, theta, reinterpret_cast<cudaStream_t>(stream),
-                                                   &st);
-    if (st != FE_OK) return st;
-    return done(e, "fe_linear_qk_norm_rope_bf16");
+    return qk_norm_rope_call("fe_linear_qk_norm_rope_bf16", x, w, q_w, k_w, positions, qkv, m, k, q_heads, kv_heads,
+                             head_dim, one_plus, eps, theta, nullptr, 0, stream);
+}
+
+fe_status fe_linear_qk_norm_rope_scaled_bf16(const void *x, const void *w, const float *q_w, const float *k_w,
+                                             const int32_t *positions, void *qkv, int64_t m, int64_t k,
+                                             int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t one_plus,
+                                             float eps, float theta, const float *row_ss, int32_t ss_parts,
+                                             fe_stream_t stream)
+{
+    if (ss_parts < 1 || ss_parts > 8)
+        return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_scaled_bf16: ss_parts must be 1..8");
+    if (m > 0 && !row_ss) return fail(FE_ERR_INVALID_ARGUMENT, "fe_linear_qk_norm_rope_scaled_bf16: null pointer");
+    return qk_norm_rope_call("fe_linear_qk_norm_rope_scaled_bf16", x, w, q_w, k_w, positions, qkv, m, k, q_heads,
+                             kv_heads, head_dim, one_plus, eps, theta, row_ss, ss_parts, stream);
 }
 
 fe_status fe_token_positions(const int32_t *cu_seqlens, int32_t batch, int32_t *positions, fe_stream_t stream)

@@ -120,6 +120,7 @@ struct fe_engine {
     // activations, sized for the largest batch seen
     DevBuf h32, h16, qkv, attn, y32, ff;
     DevBuf ln_ws;  // row-statistics exchange of the fused linear + LayerNorm (zero-filled when allocated)
+    DevBuf rss;    // fp32 [T][parts]: row sums of squares of the deferred pre-norm RMSNorm (Qwen3 shapes)
     int64_t cap_tokens = 0;
     // per-call inputs for the host path
     DevBuf d_ids, d_cu, d_out;
@@ -414,11 +415,24 @@ fe_status ensure_activations_rms(fe_engine *e, int64_t T)
     FE_TRY_CUDA(e->ff.ensure(cap * F * 2));
     FE_TRY_CUDA(e->hfin.ensure(cap * D * 4));
     FE_TRY_CUDA(e->tpos.ensure(cap * 4));
+    FE_TRY_CUDA(e->rss.ensure(cap * 8 * 4));
     const size_t ws = fe::linear_layernorm_stats_bytes(cap, static_cast<int64_t>(D));
     FE_TRY_CUDA(e->ln_ws.ensure(ws));
     FE_TRY_CUDA(cudaMemset(e->ln_ws.p, 0, ws));
     e->cap_tokens = cap;
     return FE_OK;
+}
+
+// FE_RMS_DEFER=0 keeps the pre-norm RMSNorm of o_proj / down_proj inside those GEMMs (row
+// statistics exchanged between the CTA pairs of a row, second pass over TMEM) instead of
+// deferring the row factor to the next projection's epilogue (for comparison).
+bool rms_defer_enabled()
+{
+    static const bool on = [] {
+        const char *v = getenv("FE_RMS_DEFER");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 bool qkrope_fuse_enabled()
@@ -477,11 +491,18 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
     void *x16 = e->h16.p, *qkv = e->qkv.p, *attn = e->attn.p, *ff = e->ff.p;
     const float eps = c.rms_norm_eps;
     const float qscale = c.query_scale > 0.f ? c.query_scale : 1.0f / sqrtf(static_cast<float>(hd));
+    // Qwen3: the RMSNorms that follow o_proj and down_proj are deferred.  Those GEMMs write
+    // bf16(h * w) and each row's partial sums of h^2 (rss); the next projection (gate_up,
+    // or the next layer's QKV) multiplies its product's rows by 1 / rms(h).  Layer 0's QKV
+    // reads rows normalised by the row kernel (no factor).
+    const int ss_parts = fe::linear_rms_deferred_parts(D);
+    const bool defer = !gemma && rms_defer_enabled() && D % 256 == 0 && D <= 2048;
+    float *rss = defer ? e->rss.as<float>() : nullptr;
     auto gemm = [&](const void *x, const DevBuf &w, const float *bias, const float *res, void *y, int64_t n, int64_t k,
-                    int epi, int dtype) -> fe_status {
+                    int epi, int dtype, const float *row_ss = nullptr) -> fe_status {
         Scope sc(e, CAT_GEMM, s);
         fe_status st = FE_OK;
-        cudaError_t err = fe::launch_linear_bf16(x, w.p, bias, res, y, T, n, k, epi, dtype, s, &st);
+        cudaError_t err = fe::launch_linear_bf16(x, w.p, bias, res, y, T, n, k, epi, dtype, s, &st, row_ss, ss_parts, eps);
         if (st != FE_OK) return st;
         return fe::check_cuda(err, "linear");
     };
@@ -494,6 +515,16 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
                                                       out16, T, n, k, eps, e->ln_ws.p, nullptr, s, &st, true);
         if (st != FE_OK) return st;
         return fe::check_cuda(err, "linear+RMSNorm");
+    };
+    // the deferred form: h32 <- x W^T + h32, out16 <- bf16(h32 * norm_w), rss <- row sums of squares
+    auto linear_rms_deferred = [&](const void *x, const DevBuf &w, const DevBuf &norm_w, float *h, void *out16,
+                                   int64_t n, int64_t k) -> fe_status {
+        Scope sc(e, CAT_GEMM, s, "fe.linear_rmsnorm_deferred");
+        fe_status st = FE_OK;
+        cudaError_t err = fe::launch_linear_rms_deferred(x, w.p, e->zero_bias.as<float>(), norm_w.as<float>(), h, out16,
+                                                         rss, T, n, k, s, &st);
+        if (st != FE_OK) return st;
+        return fe::check_cuda(err, "linear+deferred RMSNorm");
     };
     {
         Scope sc(e, CAT_OTHER, s, "fe.embed_scale");
@@ -515,6 +546,7 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
     for (int l = 0; l < c.layers; ++l) {
         const RLayer &L = e->rlayers[l];
         const bool last = l + 1 == c.layers;
+        const float *in_ss = defer && l > 0 ? rss : nullptr;  // this layer's input still needs 1 / rms
         if (fuse_rope) {
             // QKV projection with the q/k norms and RoPE in its epilogue
             Scope sc(e, CAT_GEMM, s, "fe.qkv_qk_norm_rope");
@@ -522,11 +554,11 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
             cudaError_t err = fe::launch_linear_qk_norm_rope(x16, L.wqkv.p, qkv, T, D, c.q_heads, c.kv_heads,
                                                              static_cast<int>(hd), L.q_norm.as<float>(),
                                                              L.k_norm.as<float>(), e->tpos.as<int32_t>(), gemma, eps,
-                                                             layer_theta(c, l), s, &st);
+                                                             layer_theta(c, l), s, &st, in_ss, ss_parts);
             if (st != FE_OK) return st;
             FE_TRY_CUDA(err);
         } else {
-            FE_TRY(gemm(x16, L.wqkv, nullptr, nullptr, qkv, QKV, D, FE_EPI_NONE, FE_DTYPE_BF16));
+            FE_TRY(gemm(x16, L.wqkv, nullptr, nullptr, qkv, QKV, D, FE_EPI_NONE, FE_DTYPE_BF16, in_ss));
             Scope sc(e, CAT_OTHER, s, "fe.qk_norm_rope");
             FE_TRY_CUDA(fe::launch_qk_norm_rope(qkv, cu, batch, T, c.q_heads, c.kv_heads, static_cast<int>(hd),
                                                 L.q_norm.as<float>(), L.k_norm.as<float>(), gemma, eps,
@@ -541,7 +573,21 @@ fe_status forward_rms(fe_engine *e, const int32_t *ids, const int32_t *cu, const
             FE_TRY_CUDA(err);
         }
         const float *next_norm = last ? e->final_norm.as<float>() : e->rlayers[l + 1].in_norm.as<float>();
-        if (!gemma) {
+        if (!gemma && defer) {
+            // x <- x + attn Wo^T, x16 <- bf16(x * post_attn_norm) and the row sums of squares;
+            // gate_up applies the post-attention RMSNorm's row factor
+            FE_TRY(linear_rms_deferred(attn, L.wo, L.post_attn_norm, h32, x16, D, AO));
+            FE_TRY(gemm(x16, L.wgu, nullptr, nullptr, ff, 2 * F, D, FE_EPI_SWIGLU, FE_DTYPE_BF16, rss));
+            // x <- x + ff Wd^T, x16 <- bf16(x * next input norm) for the next layer's QKV (the
+            // final norm: below, in fp32, from h32)
+            FE_TRY(linear_rms_deferred(ff, L.wd, last ? e->final_norm : e->rlayers[l + 1].in_norm, h32,
+                                       last ? nullptr : x16, D, F));
+            if (last) {
+                Scope sc(e, CAT_OTHER, s, "fe.rms_norm");
+                FE_TRY_CUDA(fe::launch_rms_norm_rows(h32, next_norm, false, eps, T, static_cast<int>(D), fin, nullptr,
+                                                     s));
+            }
+        } else if (!gemma) {
             // x <- x + attn Wo^T and the post-attention RMSNorm into x16, one fused step
             FE_TRY(linear_rms(attn, L.wo, L.post_attn_norm, h32, x16, D, AO));
             FE_TRY(gemm(x16, L.wgu, nullptr, nullptr, ff, 2 * F, D, FE_EPI_SWIGLU, FE_DTYPE_BF16));

@@ -70,9 +70,13 @@ fe_status make_tmap_heads(CUtensorMap *map, const void *base, uint64_t heads, ui
                           uint32_t box_rows);
 
 // ---- launchers (no argument validation; the C ABI validates) ----
+// row_ss (optional): deferred RMSNorm row scale of the input, [m][ss_parts] partial sums of
+// squares from launch_linear_rms_deferred; each accumulator row i is multiplied by
+// 1 / sqrt(sum_p row_ss[i][p] / k + ss_eps) before the epilogue.
 cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias,
                                const float *residual, void *y, int64_t m, int64_t n, int64_t k,
-                               int epilogue, int y_dtype, cudaStream_t s, fe_status *st);
+                               int epilogue, int y_dtype, cudaStream_t s, fe_status *st,
+                               const float *row_ss = nullptr, int ss_parts = 0, float ss_eps = 0.f);
 // True when launch_linear_layernorm runs the step as linear_ln_cluster (LayerNorm, n a
 // multiple of 256 from 512 to 1024, k a multiple of 64; by default only where the pair kernel
 // would not fuse: pair_fused is that decision).
@@ -84,6 +88,16 @@ bool ln_cluster_applies(int64_t n, int64_t k, bool rms, bool pair_fused);
 cudaError_t launch_linear_qk_norm_rope(const void *x, const void *w, void *y, int64_t m, int64_t k, int q_heads,
                                        int kv_heads, int head_dim, const float *q_w, const float *k_w,
                                        const int32_t *pos, bool one_plus, float eps, float theta, cudaStream_t s,
+                                       fe_status *st, const float *row_ss = nullptr, int ss_parts = 0);
+// Pre-norm projection + residual with the RMSNorm deferred to the consumer:
+//     h32 <- (x W^T + bias) + h32,   h16 <- bf16(h32 * gamma) (h16 may be null),
+//     row_ss[i][p] <- sum of h32[i][j]^2 over part p of the columns (linear_rms_deferred_parts(n)
+// parts); the next projection of h16 takes row_ss (launch_linear_bf16 /
+// launch_linear_qk_norm_rope) and applies the factor 1 / sqrt(mean(h32^2) + eps) per row.
+// n a multiple of 256, at most 2048.
+int linear_rms_deferred_parts(int64_t n);
+cudaError_t launch_linear_rms_deferred(const void *x, const void *w, const float *bias, const float *gamma, float *h32,
+                                       void *h16, float *row_ss, int64_t m, int64_t n, int64_t k, cudaStream_t s,
                                        fe_status *st);
 // h32 <- LayerNorm((x W^T + bias) + h32) * gamma + beta; h16 <- bf16 of it (h16 may be
 // null).  stats / y_fallback come from linear_layernorm_split_workspace; the stats

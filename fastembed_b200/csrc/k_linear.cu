@@ -70,6 +70,13 @@ __device__ __forceinline__ float act(float x, int epi)
 // bf16 qkv buffer.  Columns [0, q_cols) are query heads, [q_cols, k_end) key heads, the
 // rest value heads (stored as they are); every head-group boundary falls on a 256-column
 // tile boundary, so a tile is all query, all key or all value.
+//
+// The same parameter block carries an optional deferred row scale (any epilogue): when
+// row_ss is set, every accumulator row i is first multiplied by
+//     s_i = 1 / sqrt(sum_p row_ss[i][p] * ss_inv_d + ss_eps),
+// the RMSNorm factor of a pre-norm input whose per-column weight the producer already
+// applied (x16 = bf16(h * w), row_ss = partial sums of h^2: linear_ln_tcgen05_pair's
+// deferred form).  Null: no scaling.
 struct RopeParams {
     const int32_t *pos;    // [M] position of each row's token in its sentence
     const float *qw, *kw;  // [hd] q_norm / k_norm weights
@@ -77,7 +84,22 @@ struct RopeParams {
     int hd;                // 128 or 256
     int one_plus;          // Gemma3 weight form (1 + w)
     float eps, log2_theta;
+    const float *row_ss;   // [M][ss_parts] partial sums of squares of the input rows, or null
+    int ss_parts;
+    float ss_inv_d, ss_eps;
 };
+
+// s_i of the deferred row scale (1 without one, and for rows past M)
+__device__ __forceinline__ float deferred_row_scale(const RopeParams &rp, int row, int M)
+{
+    if (rp.row_ss == nullptr || row >= M) return 1.f;
+    const float *p = rp.row_ss + static_cast<size_t>(row) * rp.ss_parts;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = i < rp.ss_parts ? __ldg(p + i) : 0.f;  // independent loads
+    const float t = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    return 1.0f / sqrtf(t * rp.ss_inv_d + rp.ss_eps);
+}
 
 // The epilogue warps (threads 64 .. 64 + nthreads of the CTA) fill the CTA's table of
 // inverse RoPE frequencies theta^(-2i / hd), i < hd / 2, then meet at named barrier 1.
@@ -97,7 +119,7 @@ __device__ __forceinline__ void fill_rope_table(float *inv_tab, const RopeParams
 template <int BN, int HD>
 __device__ __forceinline__ void drain_qk_rope(uint32_t t_row, int row, int store_row, int n0, int M,
                                               const RopeParams &rp, const float *inv_tab, const CUtensorMap *tm_y,
-                                              uint8_t *bufs, int lane)
+                                              uint8_t *bufs, int lane, float sc)
 {
     static_assert(BN % HD == 0, "a tile holds whole heads");
     const float *wv = n0 < rp.q_cols ? rp.qw : rp.kw;
@@ -121,7 +143,8 @@ __device__ __forceinline__ void drain_qk_rope(uint32_t t_row, int row, int store
             }
         }
         const float ss = ss0 + ss1;
-        const float r = rsqrtf(ss / static_cast<float>(HD) + rp.eps);
+        // with a deferred row scale sc the head's values are sc * acc: norm factor of those, times sc
+        const float r = sc * rsqrtf(sc * sc * ss / static_cast<float>(HD) + rp.eps);
 #pragma unroll 1
         for (int sl = 0; sl < HD / 128; ++sl) {
             if (lane == 0) bulk_wait_read<0>();  // the slabs' previous stores have read shared memory
@@ -183,7 +206,7 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
                                                   const float *__restrict__ bias,
                                                   const float *__restrict__ residual, int epi,
                                                   const CUtensorMap *tm_y, uint8_t *bufs, int &pp, int lane,
-                                                  const RopeParams &rp, const float *inv_tab)
+                                                  const RopeParams &rp, const float *inv_tab, float sc)
 {
     if constexpr (OUT_BF16) {
         if (epi == E_QKROPE) {
@@ -191,13 +214,13 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
             // only, and the launcher gives them no other
             if constexpr (BN >= 256) {
                 if (n0 < rp.k_end) {
-                    if (rp.hd == 128) drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
-                    else drain_qk_rope<BN, 256>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
+                    if (rp.hd == 128) drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane, sc);
+                    else drain_qk_rope<BN, 256>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane, sc);
                     return;
                 }
             } else if constexpr (BN == 128) {
                 if (n0 < rp.k_end && rp.hd == 128) {
-                    drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane);
+                    drain_qk_rope<BN, 128>(t_row, row, store_row, n0, M, rp, inv_tab, tm_y, bufs, lane, sc);
                     return;
                 }
             }
@@ -220,9 +243,14 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
                         float a0 = __uint_as_float(g[j]), a1 = __uint_as_float(g[j + 1]);
+                        float b0 = __uint_as_float(u[j]), b1 = __uint_as_float(u[j + 1]);
+                        if (rp.row_ss != nullptr) {  // warp-uniform: no cost without a row scale
+                            mul_f32x2(a0, a1, sc, sc);
+                            mul_f32x2(b0, b1, sc, sc);
+                        }
                         if (epi == E_SWIGLU) silu_fast2(a0, a1);
                         else gelu_tanh_fast2(a0, a1);
-                        mul_f32x2(a0, a1, __uint_as_float(u[j]), __uint_as_float(u[j + 1]));
+                        mul_f32x2(a0, a1, b0, b1);
                         o[32 * hb + j] = a0;
                         o[32 * hb + j + 1] = a1;
                     }
@@ -262,6 +290,10 @@ __device__ __forceinline__ void drain_accumulator(uint32_t t_row, int row, int s
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; ++j) f[h * 32 + j] = __uint_as_float(v[j]);
+        }
+        if (rp.row_ss != nullptr) {  // warp-uniform: no cost without a row scale
+#pragma unroll
+            for (int j = 0; j < CHUNK; ++j) f[j] *= sc;
         }
         const int col0 = n0 + c;
         if (epi != E_NONE) {
@@ -483,18 +515,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         int pp = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             if (*abort_flag) break;
+            const int m0 = (tile / n_tiles) * BM;
+            const int n0 = (tile % n_tiles) * BN;
+            const int row = m0 + q * 32 + lane;
+            // the row's deferred RMSNorm factor: its loads overlap the wait for the accumulator
+            const float sc = deferred_row_scale(rp, row, M);
             if (!mbar_wait(&acc_full[acc], acc_phase)) {
                 report(status, DEV_TIMEOUT);
                 *abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            const int m0 = (tile / n_tiles) * BM;
-            const int n0 = (tile % n_tiles) * BN;
-            const int row = m0 + q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
             drain_accumulator<BN, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
-                                            lane, rp, inv_tab);
+                                            lane, rp, inv_tab, sc);
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
             acc ^= 1;
@@ -714,18 +748,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<P_STAGES, EP
         int pp = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs) {
             if (*abort_flag) break;
+            const int m0 = (tile / n_tiles) * 256 + static_cast<int>(rank) * 128;
+            const int n0 = (tile % n_tiles) * P_BN + h * COLS;
+            const int row = m0 + q * 32 + lane;
+            // the row's deferred RMSNorm factor: its loads overlap the wait for the accumulator
+            const float sc = deferred_row_scale(rp, row, M);
             if (!mbar_wait(&acc_full[acc], acc_phase)) {
                 report(status, DEV_TIMEOUT);
                 *abort_flag = 1;
                 break;
             }
             tc_fence_after();
-            const int m0 = (tile / n_tiles) * 256 + static_cast<int>(rank) * 128;
-            const int n0 = (tile % n_tiles) * P_BN + h * COLS;
-            const int row = m0 + q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN + h * COLS;
             drain_accumulator<COLS, OUT_BF16>(t_row, row, m0 + q * 32, n0, M, N, bias, residual, epi, &tm_y, bufs, pp,
-                                              lane, rp, inv_tab);
+                                              lane, rp, inv_tab, sc);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(leader_acc_empty[acc]);
@@ -804,7 +840,10 @@ struct LnParams {
     float eps;
     int nparts;                 // statistics partials per row = N / COLS
     int rms;                    // 0: LayerNorm, h32 <- the normalised rows (post-norm);
-                                // 1: RMSNorm, h32 <- x itself, h16 <- x / rms(x) * gamma (pre-norm)
+                                // 1: RMSNorm, h32 <- x itself, h16 <- x / rms(x) * gamma (pre-norm);
+                                // 2: deferred RMSNorm, h32 <- x, h16 <- x * gamma, and the row's sum of
+                                //    x^2 over each part into ((float *) stats)[row * nparts + part]:
+                                //    the consumer applies 1 / rms(x) (no exchange, one pass)
 };
 
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v)
@@ -950,6 +989,111 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
             }
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN + h * COLS;
+
+            if (p.rms == 2) {
+                // ---- deferred RMSNorm, one pass per 32-column chunk: x = (acc + bias) + residual,
+                // its squares summed, x TMA-stored as fp32 from the residual's own slab and
+                // bf16(x * gamma) from the bf16 slab.  Bulk groups per chunk c: F(c), then B(c).
+                float ss4[4] = {0.f, 0.f, 0.f, 0.f};
+                bool ok = true;
+                uint32_t v[2][32];
+                tmem_ld_x32(t_row, v[0]);
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    const int b = c % SLABS;
+                    uint32_t(&cur)[32] = v[c & 1];
+                    tmem_wait_ld_regs(cur);
+                    if (c + 1 < CH) {
+                        tmem_ld_x32(t_row + (c + 1) * 32, v[(c + 1) & 1]);
+                        if (SLABS == 2) {  // the other slab held chunk c - 1's output: F(c - 1) has read it
+                            if (lane == 0) {
+                                if (c >= 1) bulk_wait_read<1>();
+                                load_res((c + 1) % SLABS, c0 + 32 * (c + 1), row0);
+                            }
+                            inflight |= 1u << ((c + 1) % SLABS);
+                        }
+                    }
+                    if (!mbar_wait(&rbar[b], (rpar >> b) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    rpar ^= 1u << b;
+                    inflight &= ~(1u << b);
+                    uint8_t *fs = wb + b * 4096;
+                    const uint8_t *rs = fs + lane * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint4 r = *reinterpret_cast<const uint4 *>(rs + ((j ^ (lane & 7)) << 4));
+                        const float4 bb = *reinterpret_cast<const float4 *>(vb + c * 32 + 4 * j);
+                        float x0 = __uint_as_float(cur[4 * j + 0]), x1 = __uint_as_float(cur[4 * j + 1]);
+                        float x2 = __uint_as_float(cur[4 * j + 2]), x3 = __uint_as_float(cur[4 * j + 3]);
+                        add_f32x2(x0, x1, bb.x, bb.y);
+                        add_f32x2(x2, x3, bb.z, bb.w);
+                        add_f32x2(x0, x1, __uint_as_float(r.x), __uint_as_float(r.y));
+                        add_f32x2(x2, x3, __uint_as_float(r.z), __uint_as_float(r.w));
+                        fma_f32x2v(ss4[0], ss4[1], x0, x1, x0, x1, ss4[0], ss4[1]);
+                        fma_f32x2v(ss4[2], ss4[3], x2, x3, x2, x3, ss4[2], ss4[3]);
+                        cur[4 * j + 0] = __float_as_uint(x0);
+                        cur[4 * j + 1] = __float_as_uint(x1);
+                        cur[4 * j + 2] = __float_as_uint(x2);
+                        cur[4 * j + 3] = __float_as_uint(x3);
+                    }
+                    __syncwarp();  // every lane has read the residual: the slab takes the fp32 output
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<uint4 *>(fs + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                            make_uint4(cur[4 * j + 0], cur[4 * j + 1], cur[4 * j + 2], cur[4 * j + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d_hint(&tm_h, fs, c0 + c * 32, row0, stream_policy);
+                        bulk_commit();
+                    }
+                    if (write16) {
+                        if (lane == 0) bulk_wait_read<1>();  // B(c - 1) has read the bf16 slab
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float4 g0 = *reinterpret_cast<const float4 *>(vg + c * 32 + 8 * j);
+                            const float4 g1 = *reinterpret_cast<const float4 *>(vg + c * 32 + 8 * j + 4);
+                            const uint32_t *xv = cur + 8 * j;
+                            *reinterpret_cast<uint4 *>(hs + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = make_uint4(
+                                pack_bf16x2(__uint_as_float(xv[0]) * g0.x, __uint_as_float(xv[1]) * g0.y),
+                                pack_bf16x2(__uint_as_float(xv[2]) * g0.z, __uint_as_float(xv[3]) * g0.w),
+                                pack_bf16x2(__uint_as_float(xv[4]) * g1.x, __uint_as_float(xv[5]) * g1.y),
+                                pack_bf16x2(__uint_as_float(xv[6]) * g1.z, __uint_as_float(xv[7]) * g1.w));  // 64B swizzle
+                        }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                    }
+                    if (lane == 0) {  // an empty group keeps the F / B alternation when bf16 is not written
+                        if (write16) tma_store_2d_hint(&tm_h16, hs, c0 + c * 32, row0, stream_policy);
+                        bulk_commit();
+                    }
+                    if (SLABS == 1 && c + 1 < CH) {  // the only slab held chunk c's output: F(c) has read it
+                        if (lane == 0) {
+                            bulk_wait_read<1>();
+                            load_res(0, c0 + 32 * (c + 1), row0);
+                        }
+                        inflight |= 1u;
+                    }
+                }
+                tmem_wait_ld();
+                if (!ok) {
+                    report(status, DEV_TIMEOUT);
+                    *abort_flag = 1;
+                    break;
+                }
+                if (row < M)
+                    reinterpret_cast<float *>(p.stats)[static_cast<size_t>(row) * p.nparts + part] =
+                        (ss4[0] + ss4[1]) + (ss4[2] + ss4[3]);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(leader_acc_empty[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+                continue;
+            }
 
             // ---- pass 1: x = (acc + bias) + residual back into TMEM; per-chunk mean / M2
             float cm[CH], cq_sum = 0.f;
@@ -1355,17 +1499,27 @@ cudaError_t launch_linear_any(const void *x, const void *w, const float *bias, c
 }  // namespace
 
 cudaError_t launch_linear_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
-                               int64_t m, int64_t n, int64_t k, int epilogue, int y_dtype, cudaStream_t s, fe_status *st)
+                               int64_t m, int64_t n, int64_t k, int epilogue, int y_dtype, cudaStream_t s, fe_status *st,
+                               const float *row_ss, int ss_parts, float ss_eps)
 {
-    return launch_linear_any(x, w, bias, residual, y, m, n, k, epilogue, y_dtype, s, st, RopeParams{});
+    RopeParams rp{};
+    rp.row_ss = row_ss;
+    rp.ss_parts = ss_parts;
+    rp.ss_inv_d = 1.0f / static_cast<float>(k);
+    rp.ss_eps = ss_eps;
+    return launch_linear_any(x, w, bias, residual, y, m, n, k, epilogue, y_dtype, s, st, rp);
 }
 
 cudaError_t launch_linear_qk_norm_rope(const void *x, const void *w, void *y, int64_t m, int64_t k, int q_heads,
                                        int kv_heads, int head_dim, const float *q_w, const float *k_w,
                                        const int32_t *pos, bool one_plus, float eps, float theta, cudaStream_t s,
-                                       fe_status *st)
+                                       fe_status *st, const float *row_ss, int ss_parts)
 {
-    RopeParams rp;
+    RopeParams rp{};
+    rp.row_ss = row_ss;
+    rp.ss_parts = ss_parts;
+    rp.ss_inv_d = 1.0f / static_cast<float>(k);
+    rp.ss_eps = eps;
     rp.pos = pos;
     rp.qw = q_w;
     rp.kw = k_w;
@@ -2072,5 +2226,57 @@ cudaError_t launch_linear_layernorm(const void *x, const void *w, const float *b
 }  // namespace fe
 
 namespace fe {
+
+int linear_rms_deferred_parts(int64_t n) { return static_cast<int>(n / LnCfg<5, 4, 2>::COLS); }
+
+cudaError_t launch_linear_rms_deferred(const void *x, const void *w, const float *bias, const float *gamma, float *h32,
+                                       void *h16, float *row_ss, int64_t m, int64_t n, int64_t k, cudaStream_t s,
+                                       fe_status *st)
+{
+    *st = FE_OK;
+    if (m == 0 || n == 0) return cudaSuccess;
+    const int n_tiles = static_cast<int>(n / P_BN);
+    if (n % P_BN != 0 || n_tiles > kMaxLnParts) {
+        *st = fail(FE_ERR_UNSUPPORTED, "linear + deferred RMSNorm: n must be a multiple of 256, at most 2048");
+        return cudaSuccess;
+    }
+    const LnVariant var = pick_ln_variant(k);
+    static_assert(LnCfg<5, 4, 2>::COLS == LnCfg<6, 4, 1>::COLS, "one partial count for both variants");
+    const int tiles = static_cast<int>((m + 255) / 256) * n_tiles;
+    // no pair waits for another in this form; the grid is still a multiple of n_tiles, so
+    // that every tile of a pair has the same columns
+    int pairs = std::min(var.resident(), current_sm_count() / 2);
+    pairs = pairs / n_tiles * n_tiles;
+    if (pairs > tiles) pairs = tiles;
+    if (pairs < n_tiles) {
+        *st = fail(FE_ERR_UNSUPPORTED, "linear + deferred RMSNorm: too few resident CTA pairs");
+        return cudaSuccess;
+    }
+    CUtensorMap tx, tw, th, th16;
+    fe_status r = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, k, k, BM, BK);
+    if (r == FE_OK) r = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, k, k, 128, BK);
+    if (r == FE_OK) r = make_tmap_2d(&th, h32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, n, n, 32, 32);
+    if (r == FE_OK)
+        r = h16 ? make_tmap_2d(&th16, h16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, n, n, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_64B)
+                : make_tmap_2d(&th16, h32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, n, n, 32, 32);  // not used
+    if (r != FE_OK) {
+        *st = r;
+        return cudaSuccess;
+    }
+    LnParams p;
+    p.bias = bias;
+    p.gamma = gamma;
+    p.beta = gamma;  // read into shared memory, unused
+    p.stats = reinterpret_cast<unsigned long long *>(row_ss);
+    p.epoch = 1;
+    p.eps = 0.f;
+    p.nparts = static_cast<int>(n / var.cols);
+    p.rms = 2;
+    const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
+    return launch_k(var.kern, dim3(2 * pairs), dim3(var.threads), var.smem, s, tx, tw, th, th16, M, N, K, p,
+                    h16 != nullptr ? 1 : 0, current_device_status_word());
+}
+
 cudaError_t set_wait_limit_linear(uint64_t ns) { return set_wait_limit_this_file(ns); }
 }  // namespace fe

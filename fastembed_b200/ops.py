@@ -178,6 +178,32 @@ def linear_rmsnorm(x, w, bias, rms_w, h32, eps, workspace=None, want_h16=True):
     return h32, h16
 
 
+def linear_rmsnorm_deferred(x, w, bias, rms_w, h32, want_h16=True):
+    """Pre-norm with the RMSNorm deferred: h32 <- (x @ w.T + bias) + h32 in place; returns
+    (h32, bf16(h32 * rms_w), row_ss [m, parts] partial sums of h32^2) for a row-scaled consumer."""
+    _cuda(x, w, bias, rms_w, h32)
+    m, k = x.shape
+    n = w.shape[0]
+    parts = capi.lib().fe_linear_rmsnorm_deferred_parts(n)
+    h16 = torch.empty(m, n, dtype=torch.bfloat16, device=x.device) if want_h16 else None
+    row_ss = torch.empty(m, max(parts, 1), dtype=torch.float32, device=x.device)
+    call("fe_linear_rmsnorm_deferred_bf16", _p(x), _p(w), _p(bias), _p(rms_w), _p(h32), _p(h16), _p(row_ss), m, n, k,
+         _s(x))
+    return h32, h16, row_ss
+
+
+def linear_row_scaled(x, w, row_ss, eps, bias=None, residual=None, epilogue="none", out_dtype="bf16"):
+    """linear_bf16 with row i of x @ w.T multiplied by 1 / sqrt(sum(row_ss[i]) / k + eps) first."""
+    _cuda(x, w, row_ss, bias, residual)
+    m, k = x.shape
+    n = w.shape[0]
+    ny = n // 2 if epilogue in ("swiglu", "geglu") else n
+    y = torch.empty(m, ny, dtype=torch.bfloat16 if out_dtype == "bf16" else torch.float32, device=x.device)
+    call("fe_linear_row_scaled_bf16", _p(x), _p(w), _p(bias), _p(residual), _p(y), m, n, k, EPI[epilogue],
+         DTYPE[out_dtype], _p(row_ss), row_ss.shape[1], eps, _s(x))
+    return y
+
+
 def embed_scale(ids, word, scale):
     _cuda(ids, word)
     T = ids.numel()
@@ -232,6 +258,17 @@ def linear_qk_norm_rope(x, w, q_w, k_w, positions, q_heads, kv_heads, head_dim, 
     y = torch.empty(m, (q_heads + 2 * kv_heads) * head_dim, dtype=torch.bfloat16, device=x.device)
     call("fe_linear_qk_norm_rope_bf16", _p(x), _p(w), _p(q_w), _p(k_w), _p(positions), _p(y), m, k, q_heads,
          kv_heads, head_dim, 1 if one_plus else 0, eps, theta, _s(x))
+    return y
+
+
+def linear_qk_norm_rope_scaled(x, w, q_w, k_w, positions, q_heads, kv_heads, head_dim, eps, theta, row_ss,
+                               one_plus=False):
+    """linear_qk_norm_rope on an input whose rows still need their RMSNorm factor (row_ss)."""
+    _cuda(x, w, q_w, k_w, positions, row_ss)
+    m, k = x.shape
+    y = torch.empty(m, (q_heads + 2 * kv_heads) * head_dim, dtype=torch.bfloat16, device=x.device)
+    call("fe_linear_qk_norm_rope_scaled_bf16", _p(x), _p(w), _p(q_w), _p(k_w), _p(positions), _p(y), m, k, q_heads,
+         kv_heads, head_dim, 1 if one_plus else 0, eps, theta, _p(row_ss), row_ss.shape[1], _s(x))
     return y
 
 

@@ -218,6 +218,29 @@ fe_status fe_layernorm_dual(const float *x, const float *residual, const float *
 fe_status fe_linear_rmsnorm_bf16(const void *x, const void *w, const float *bias, const float *rms_w, float *h32,
                                  void *h16, int64_t m, int64_t n, int64_t k, float eps, void *workspace,
                                  size_t workspace_bytes, fe_stream_t stream);
+/* The same pre-norm step with the RMSNorm deferred to the next projection (Qwen3-shaped
+ * encoders; not in the reference):
+ *     h32 <- (x[m,k] · w[n,k]^T + bias) + h32                     (in place: the residual stream)
+ *     h16 <- bf16(h32 * rms_w)                                     (may be NULL)
+ *     row_ss[i][p] <- sum of h32[i][j]^2 over the p-th of fe_linear_rmsnorm_deferred_parts(n)
+ *                     equal column ranges                          (fp32 [m][parts])
+ * The next projection of h16 takes row_ss (fe_linear_row_scaled_bf16,
+ * fe_linear_qk_norm_rope_scaled_bf16) and multiplies row i of its product by
+ * 1 / sqrt(sum_p row_ss[i][p] / n + eps): the RMSNorm factor, applied after that GEMM, so
+ * this step needs no exchange of row statistics between the CTAs of a row.  n a multiple
+ * of 256 up to 2048, k % 8 == 0, bias required (zeros for models without one), 16-byte
+ * aligned pointers, no workspace. */
+fe_status fe_linear_rmsnorm_deferred_bf16(const void *x, const void *w, const float *bias, const float *rms_w,
+                                          float *h32, void *h16, float *row_ss, int64_t m, int64_t n, int64_t k,
+                                          fe_stream_t stream);
+/* Partials per row of fe_linear_rmsnorm_deferred_bf16 for n columns (0 if n is unsupported). */
+int32_t fe_linear_rmsnorm_deferred_parts(int64_t n);
+/* fe_linear_bf16 on an input whose rows still need their RMSNorm factor: row i of
+ * x · w^T is multiplied by 1 / sqrt(sum_p row_ss[i][p] / k + eps) before the epilogue
+ * (row_ss [m][ss_parts], ss_parts 1..8, from fe_linear_rmsnorm_deferred_bf16 with n = k). */
+fe_status fe_linear_row_scaled_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
+                                    int64_t m, int64_t n, int64_t k, fe_epilogue epilogue, fe_dtype y_dtype,
+                                    const float *row_ss, int32_t ss_parts, float eps, fe_stream_t stream);
 fe_status fe_linear_layernorm_workspace_bytes(int64_t m, int64_t n, size_t *bytes);
 fe_status fe_linear_layernorm_bf16(const void *x, const void *w, const float *bias, const float *gamma,
                                    const float *beta, float *h32, void *h16, int64_t m, int64_t n, int64_t k,
@@ -252,6 +275,13 @@ fe_status fe_linear_qk_norm_rope_bf16(const void *x, const void *w, const float 
                                       const int32_t *positions, void *qkv, int64_t m, int64_t k, int32_t q_heads,
                                       int32_t kv_heads, int32_t head_dim, int32_t one_plus, float eps, float theta,
                                       fe_stream_t stream);
+/* fe_linear_qk_norm_rope_bf16 on an input whose rows still need their RMSNorm factor
+ * (row_ss, ss_parts as in fe_linear_row_scaled_bf16; the same eps for both norms). */
+fe_status fe_linear_qk_norm_rope_scaled_bf16(const void *x, const void *w, const float *q_w, const float *k_w,
+                                             const int32_t *positions, void *qkv, int64_t m, int64_t k,
+                                             int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t one_plus,
+                                             float eps, float theta, const float *row_ss, int32_t ss_parts,
+                                             fe_stream_t stream);
 /* positions[t] = position of token t in its sentence (0, 1, ...) for the packed batch of
  * cu_seqlens [batch + 1]: the positions fe_linear_qk_norm_rope_bf16 reads. */
 fe_status fe_token_positions(const int32_t *cu_seqlens, int32_t batch, int32_t *positions, fe_stream_t stream);

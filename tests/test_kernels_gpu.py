@@ -641,6 +641,95 @@ def test_linear_qk_norm_rope(cuda_dev, monkeypatch, pair, hd, hq, hkv, theta, on
     ops.device_status(0)
 
 
+# (m, n, k): Qwen3-0.6B's o_proj (k 2048) and down_proj (k 3072), a k = 4096 shape (the
+# one-slab configuration), a short k, 3 and 8 column tiles and a single ragged row tile
+DEFERRED_SHAPES = [(700, 1024, 2048), (1500, 1024, 3072), (333, 1024, 4096), (600, 1024, 1024), (4097, 768, 2048),
+                   (130, 2048, 2048), (1, 256, 512)]
+
+
+@pytest.mark.parametrize("m,n,k", DEFERRED_SHAPES)
+def test_linear_rmsnorm_deferred(cuda_dev, m, n, k):
+    """Pre-norm step with the RMSNorm deferred: h32 <- (x W^T + b) + h32, h16 <- bf16(h32 * w)
+    and the row sums of h32^2 per 256-column part, against fp32 torch; twice on the same
+    buffers (the sums are overwritten, not accumulated)."""
+    from fastembed_b200 import capi, ops
+    x, w, b, res, gam, _ = _linear_ln_inputs(m, n, k, 5 * m + n + k, cuda_dev)
+    y = (x.float() @ w.float().T + b) + res
+    parts = capi.lib().fe_linear_rmsnorm_deferred_parts(n)
+    assert parts == n // 256
+    ref_ss = (y * y).view(m, parts, n // parts).sum(-1)
+    ref16 = y * gam
+    for _ in range(2):
+        h32, h16, ss = ops.linear_rmsnorm_deferred(x, w, b, gam, res.clone())
+        torch.cuda.synchronize()
+        assert float((h32 - y).abs().max()) < 1e-3
+        err = (h16.float() - ref16).abs()
+        assert bool((err <= ref16.abs() * 2.0 ** -7 + 1e-4).all()), float(err.max())
+        assert float(((ss - ref_ss).abs() / ref_ss).max()) < 1e-4
+    h32n, none16, ss2 = ops.linear_rmsnorm_deferred(x, w, b, gam, res.clone(), want_h16=False)
+    torch.cuda.synchronize()
+    assert none16 is None
+    assert torch.equal(h32n, h32) and torch.equal(ss2, ss)
+    ops.device_status(0)
+
+
+@pytest.mark.parametrize("epi,m,F,k", [("swiglu", 700, 3072, 1024), ("swiglu", 77, 1152, 768), ("none", 600, 512, 1024),
+                                       ("none", 100, 384, 256)])
+def test_linear_row_scaled(cuda_dev, monkeypatch, epi, m, F, k):
+    """A projection of rows that still need their RMSNorm factor: row i of x W^T is scaled by
+    1 / sqrt(sum(row_ss[i]) / k + eps) before the epilogue, against fp32 torch on the
+    normalised rows; the 2-CTA and the 1-CTA kernels."""
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(m + F + k + 1)
+    h = torch.randn(m, k, device=cuda_dev, generator=g) * 3 + 0.2
+    wn = torch.randn(k, device=cuda_dev, generator=g) * 0.5 + 1
+    parts = max(1, k // 256)
+    row_ss = (h * h).view(m, parts, k // parts).sum(-1).contiguous()
+    x = (h * wn).to(torch.bfloat16)  # the producer's bf16(h * w)
+    xn = h * torch.rsqrt((h * h).mean(-1, keepdim=True) + 1e-6) * wn  # the normalised rows
+    if epi == "swiglu":
+        wg = (torch.randn(F, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+        wu = (torch.randn(F, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+        wt, ref = _interleave32(wg, wu), torch.nn.functional.silu(xn @ wg.float().T) * (xn @ wu.float().T)
+    else:
+        wt = (torch.randn(F, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+        ref = xn @ wt.float().T
+    for pair in ("1", "0"):
+        monkeypatch.setenv("FE_LINEAR_PAIR", pair)
+        y = ops.linear_row_scaled(x, wt, row_ss, 1e-6, epilogue=epi)
+        torch.cuda.synchronize()
+        assert _rel_err(y, ref) < 1e-2  # bf16 input and output rounding, fast exp
+    ops.device_status(0)
+
+
+@pytest.mark.parametrize("hd,hq,hkv", [(128, 16, 8), (256, 4, 2)])
+def test_linear_qk_norm_rope_scaled(cuda_dev, hd, hq, hkv):
+    """The QKV projection with q/k norms and RoPE on rows that still need their RMSNorm
+    factor equals (within bf16 rounding) the same projection of the normalised rows."""
+    from fastembed_b200 import ops
+    g = torch.Generator(device=cuda_dev).manual_seed(hd + hq + 7)
+    lens = [1, 128, 129, 7, 600]
+    T, D = sum(lens), 1024
+    N = (hq + 2 * hkv) * hd
+    h = torch.randn(T, D, device=cuda_dev, generator=g) * 2 - 0.3
+    wn = torch.randn(D, device=cuda_dev, generator=g) * 0.3 + 1
+    row_ss = (h * h).view(T, 4, D // 4).sum(-1).contiguous()
+    x = (h * wn).to(torch.bfloat16)
+    xn = (h * torch.rsqrt((h * h).mean(-1, keepdim=True) + 1e-6) * wn).to(torch.bfloat16)
+    w = (torch.randn(N, D, device=cuda_dev, generator=g) * 0.05).to(torch.bfloat16)
+    qw = torch.randn(hd, device=cuda_dev, generator=g) * 0.3 + 1
+    kw = torch.randn(hd, device=cuda_dev, generator=g) * 0.3 + 1
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda_dev)
+    pos = ops.token_positions(cu)
+    y = ops.linear_qk_norm_rope_scaled(x, w, qw, kw, pos, hq, hkv, hd, 1e-6, 1e6, row_ss).float()
+    ref = ops.linear_qk_norm_rope(xn, w, qw, kw, pos, hq, hkv, hd, 1e-6, 1e6).float()
+    torch.cuda.synchronize()
+    kc = (hq + hkv) * hd
+    assert float((y[:, :kc] - ref[:, :kc]).abs().max()) < 2e-2 * float(ref[:, :kc].abs().max())
+    assert float((y[:, kc:] - ref[:, kc:]).abs().max()) < 2e-2 * float(ref[:, kc:].abs().max())
+    ops.device_status(0)
+
+
 def test_linear_qk_norm_rope_rejects_unaligned_heads(cuda_dev):
     import ctypes as C
     from fastembed_b200 import capi
