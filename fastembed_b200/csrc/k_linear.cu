@@ -863,7 +863,9 @@ __device__ __forceinline__ unsigned long long tag(float v, unsigned epoch)
     return (static_cast<unsigned long long>(__float_as_uint(v)) << 32) | epoch;
 }
 
-template <int STAGES, int EPI_WARPS, int SLABS>
+// DEFER: the deferred RMSNorm form (LnParams::rms == 2), its own instantiation so that the
+// LayerNorm / RMSNorm forms keep their code unchanged.
+template <int STAGES, int EPI_WARPS, int SLABS, bool DEFER>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WARPS, SLABS>::THREADS, 1)
     linear_ln_tcgen05_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_h16,
@@ -990,7 +992,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(LnCfg<STAGES, EPI_WA
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * P_BN + h * COLS;
 
-            if (p.rms == 2) {
+            if constexpr (DEFER) {
                 // ---- deferred RMSNorm, one pass per 32-column chunk: x = (acc + bias) + residual,
                 // its squares summed, x TMA-stored as fp32 from the residual's own slab and
                 // bf16(x * gamma) from the bf16 slab.  Bulk groups per chunk c: F(c), then B(c).
@@ -1386,7 +1388,7 @@ cudaError_t launch_pair(const CUtensorMap &tx, const CUtensorMap &tw, const CUte
 
 // Pairs of linear_ln_tcgen05_pair<Cfg> that can be resident at once on the current
 // device (0 if unknown).
-template <class Cfg, int STAGES, int EPI_WARPS, int SLABS>
+template <class Cfg, int STAGES, int EPI_WARPS, int SLABS, bool DEFER>
 int ln_resident_pairs()
 {
     static int cached[64] = {};
@@ -1395,7 +1397,7 @@ int ln_resident_pairs()
     cudaGetDevice(&dev);
     const uint64_t ctx = current_context_id();
     if (dev < 64 && cached[dev] > 0 && cached_ctx[dev] == ctx) return cached[dev];
-    auto kern = linear_ln_tcgen05_pair<STAGES, EPI_WARPS, SLABS>;
+    auto kern = linear_ln_tcgen05_pair<STAGES, EPI_WARPS, SLABS, DEFER>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess) return 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2, 1, 1);
@@ -1582,19 +1584,21 @@ struct LnVariant {
     uint32_t smem;
     LnKernel kern;
 };
-template <int S, int E, int L>
+template <int S, int E, int L, bool DEFER = false>
 LnVariant ln_variant()
 {
     using Cf = LnCfg<S, E, L>;
-    return {&ln_resident_pairs<Cf, S, E, L>, Cf::COLS, Cf::THREADS, Cf::SMEM, &linear_ln_tcgen05_pair<S, E, L>};
+    return {&ln_resident_pairs<Cf, S, E, L, DEFER>, Cf::COLS, Cf::THREADS, Cf::SMEM,
+            &linear_ln_tcgen05_pair<S, E, L, DEFER>};
 }
 // Ring depth against residual double-buffering (shared memory holds one or the other):
 // measured per launch at n = 1024 on one B200,
 //   k = 4096, m = 26508 (LayerNorm):  6 stages / 1 slab 216 us, 5 stages / 2 slabs 221 us;
 //   k = 3072, m = 71550 (RMSNorm):    468 us and 427 us;  k = 2048: 378 us and 344 us.
 // Eight epilogue warps were slower in every case (252-545 us).
-LnVariant pick_ln_variant(int64_t k)
+LnVariant pick_ln_variant(int64_t k, bool defer = false)
 {
+    if (defer) return k >= 4096 ? ln_variant<6, 4, 1, true>() : ln_variant<5, 4, 2, true>();
     return k >= 4096 ? ln_variant<6, 4, 1>() : ln_variant<5, 4, 2>();
 }
 }  // namespace
@@ -2240,7 +2244,7 @@ cudaError_t launch_linear_rms_deferred(const void *x, const void *w, const float
         *st = fail(FE_ERR_UNSUPPORTED, "linear + deferred RMSNorm: n must be a multiple of 256, at most 2048");
         return cudaSuccess;
     }
-    const LnVariant var = pick_ln_variant(k);
+    const LnVariant var = pick_ln_variant(k, true);
     static_assert(LnCfg<5, 4, 2>::COLS == LnCfg<6, 4, 1>::COLS, "one partial count for both variants");
     const int tiles = static_cast<int>((m + 255) / 256) * n_tiles;
     // no pair waits for another in this form; the grid is still a multiple of n_tiles, so
