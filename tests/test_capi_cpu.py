@@ -70,6 +70,30 @@ def test_validation_happens_before_any_device_work(fe_lib):
     assert L.fe_set_wait_limit(0, 0) == 1  # a zero limit is refused before any device is touched
 
 
+def test_deferred_rmsnorm_entry_points_validate_before_device_work(fe_lib):
+    """The deferred pre-norm step and its row-scaled consumers reject bad shapes and
+    arguments without touching the device; the partial count is n / 256."""
+    from fastembed_b200.capi import EPI, DTYPE
+    buf = C.c_void_p(16)  # never dereferenced
+    L = fe_lib
+    assert [L.fe_linear_rmsnorm_deferred_parts(n) for n in (256, 768, 1024, 2048, 640, 2304, 0)] == [1, 3, 4, 8, 0, 0, 0]
+    # n = 640 is not a multiple of 256; k = 60 is not a multiple of 8; a null row_ss
+    assert L.fe_linear_rmsnorm_deferred_bf16(buf, buf, buf, buf, buf, buf, buf, 4, 640, 64, None) == 4
+    assert L.fe_linear_rmsnorm_deferred_bf16(buf, buf, buf, buf, buf, buf, buf, 4, 1024, 60, None) == 1
+    assert L.fe_linear_rmsnorm_deferred_bf16(buf, buf, buf, buf, buf, buf, None, 4, 1024, 64, None) == 1
+    assert L.fe_linear_rmsnorm_deferred_bf16(None, None, None, None, None, None, None, 0, 1024, 64, None) == 0
+    # ss_parts outside 1..8, or no row_ss for a non-empty input
+    for parts, rss in ((0, buf), (9, buf), (4, None)):
+        assert L.fe_linear_row_scaled_bf16(buf, buf, None, None, buf, 4, 256, 64, EPI["none"], DTYPE["bf16"], rss,
+                                           parts, 1e-6, None) == 1
+        assert L.fe_linear_qk_norm_rope_scaled_bf16(buf, buf, buf, buf, buf, buf, 4, 1024, 16, 8, 128, 0, 1e-6, 1e6,
+                                                    rss, parts, None) == 1
+    # the row-scaled linear keeps fe_linear_bf16's own checks (k = 60)
+    assert L.fe_linear_row_scaled_bf16(buf, buf, None, None, buf, 4, 256, 60, EPI["none"], DTYPE["bf16"], buf, 4, 1e-6,
+                                       None) == 1
+    assert b"fe_linear_row_scaled_bf16" in L.fe_last_error_message()
+
+
 def test_engine_create_without_gpu_fails_cleanly(fe_lib):
     import torch
     if torch.cuda.is_available():
